@@ -1,0 +1,385 @@
+"""Benchmark of the B200-native SPLADE head: fused forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+Workload (the configuration its metric is quoted on):
+B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden ~ N(0,1),
+W ~ N(0,0.02), bias ~ N(0,0.02), right-padded mask with lengths U[32,256],
+upstream grad g ~ N(0,1); seeded synthetic data standing in for SPLADE
+batches. With N GPUs the decoder is vocabulary-sharded over the ranks (the same
+total workload: strong scaling) and the partial d_hidden is all-reduced (fp32,
+NCCL).
+
+One step = head forward (mask reduction + fused GEMM/max/argmax/log1p kernel)
++ backward (sort by argmax, dH, dW, db) [+ all-reduce of dH].
+
+Prints ONE JSON line on rank 0. ``value`` is the BASELINE metric, nominal
+fwd+bwd TFLOP/s = 4*B*S*D*V / step time, with inputs resident in HBM and the
+L2 flushed (256 MiB write) before every timed step; time is the max over ranks
+of CUDA-event time. ``e2e`` is the same metric through the public module
+(SpartonHead autograd) with host->device copies of the step's inputs from
+pinned memory and a device->host read of reps inside the timed region.
+``roofline`` covers the dominant kernel (the forward): algorithmic FLOPs
+2*D*V*T (T = valid tokens) over its CUDA-event duration, against the measured
+bf16 peak. ``cpu_baseline`` times the reference torch head (oracle/torch_head.py,
+a restatement of the reference's --head torch path) on the host cores on a
+bounded sample of the same workload.
+
+``--impl reference`` times that CPU reference alone (rank 0; other ranks exit)
+and prints its line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = "fused head fwd+bwd TFLOP/s (4·B·S·D·V) & tokens/s at 1/2/4/8 B200; % of bf16 peak"
+CFG = dict(name="config 2 (BERT-base SPLADE head)", B=128, S=256, D=768, V=30522,
+           dtype=torch.bfloat16, lengths=(32, 256), bias=True, w_std=0.02)
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def nominal_flops(c) -> float:
+    return 4.0 * c["B"] * c["S"] * c["D"] * c["V"]
+
+
+def make_inputs(c, seed=0):
+    """CPU tensors of the workload (seeded; identical on every rank)."""
+    gen = torch.Generator().manual_seed(seed)
+    B, S, D, V = c["B"], c["S"], c["D"], c["V"]
+    H = torch.randn(B, S, D, generator=gen).to(c["dtype"])
+    W = (torch.randn(V, D, generator=gen) * c["w_std"]).to(c["dtype"])
+    b = (torch.randn(V, generator=gen) * 0.02).to(c["dtype"]) if c["bias"] else None
+    lo, hi = c["lengths"]
+    L = torch.randint(lo, hi + 1, (B,), generator=gen)
+    mask = (torch.arange(S)[None, :] < L[:, None]).to(torch.int64)
+    g = torch.randn(B, V, generator=gen).to(c["dtype"])
+    return H, W, b, mask, g, L
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per forward launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "fwd_tc_config2_traffic.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of this process's GPU via NVML
+    every 20 ms while active (read-only)."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, device: torch.device):
+        self.samples, self.reasons, self.max_mhz, self.err = [], set(), None, None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.err = repr(e)
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception as e:  # pragma: no cover
+                self.err = repr(e)
+                return
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0, "error": self.err}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_baseline(c, sample_rows: int, steps: int, warmup: int) -> dict:
+    from oracle.torch_head import time_fwd_bwd
+
+    _, _, _, _, _, L = make_inputs(dict(c, B=sample_rows), seed=1)
+    r = time_fwd_bwd(sample_rows, c["S"], c["D"], c["V"], L.tolist(), use_bias=c["bias"],
+                     steps=steps, warmup=warmup)
+    flops = 4.0 * sample_rows * c["S"] * c["D"] * c["V"]
+    return {"value": flops / r["seconds_per_step"] / 1e12, "unit": "TFLOP/s",
+            "cores": r["threads"], "kind": "port",
+            "sample": f"B={sample_rows} of {c['B']} rows (S={c['S']} D={c['D']} V={c['V']}), fp32, "
+                      f"torch head on host cores, {steps} steps after {warmup} warm-up",
+            "seconds_per_step": r["seconds_per_step"]}
+
+
+def run_reference_arm(args, rank: int) -> int:
+    if rank != 0:
+        return 0
+    c = CFG
+    rows = 8
+    res = cpu_baseline(c, rows, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["seconds_per_step"] * 1e3 * c["B"] / rows,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config 2: B=128 S=256 D=768 V=30522, lengths U[32,256]",
+                   "B": c["B"], "S": c["S"], "D": c["D"], "V": c["V"],
+                   "per_step_sample_rows": rows, "device": "host CPU"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+
+    import datetime
+
+    import torch.distributed as dist
+
+    from sparton_b200 import _lib
+    from sparton_b200.head import SpartonHead, VocabShard
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        group = dist.group.WORLD
+
+    c = CFG
+    B, S, D, V = c["B"], c["S"], c["D"], c["V"]
+    H, W, b, mask, g, L = make_inputs(c)
+    T = int(L.sum())
+    shard = VocabShard(V, world, rank)
+    Vs = shard.size
+    Ws = W[shard.start:shard.stop].contiguous()
+    bs = b[shard.start:shard.stop].contiguous() if b is not None else None
+    gs = g[:, shard.start:shard.stop].contiguous()
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    Hd, Wd, md, gd = H.to(dev), Ws.to(dev), mask.to(dev), gs.to(dev)
+    bd = bs.to(dev) if bs is not None else None
+    reps = torch.empty(B, Vs, dtype=c["dtype"], device=dev)
+    idx = torch.empty(B, Vs, dtype=torch.int32, device=dev)
+    dh_dtype = torch.float32 if world > 1 else c["dtype"]
+    dH = torch.empty(B, S, D, dtype=dh_dtype, device=dev)
+    dW = torch.empty(Vs, D, dtype=c["dtype"], device=dev)
+    db = torch.empty(Vs, dtype=c["dtype"], device=dev) if bd is not None else None
+    wsf = torch.empty(lib.sparton_fwd_workspace_size(B, S, D, Vs), dtype=torch.uint8, device=dev)
+    wsb = torch.empty(lib.sparton_bwd_workspace_size(B, S, D, Vs), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    dt = _lib.DTYPE[c["dtype"]]
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(k0=None, k1=None):
+        _lib.check(lib.sparton_mask_prepare(md.data_ptr(), 2, B, S, wsf.data_ptr(), wsf.numel(), sh),
+                   "mask_prepare")
+        if k0 is not None:
+            k0.record(stream)
+        _lib.check(lib.sparton_fwd_prepared(Hd.data_ptr(), Wd.data_ptr(), _lib.ptr(bd), dt, B, S, D,
+                                            Vs, reps.data_ptr(), idx.data_ptr(), wsf.data_ptr(),
+                                            wsf.numel(), sh), "fwd")
+        if k1 is not None:
+            k1.record(stream)
+        _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
+                                   Wd.data_ptr(), dt, B, S, D, Vs, dH.data_ptr(), dW.data_ptr(),
+                                   _lib.ptr(db), _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(),
+                                   wsb.numel(), sh), "bwd")
+        if world > 1:
+            dist.all_reduce(dH, group=group)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=group, device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        return float(t.item())
+
+    # ---------------------------------------------------------------- device-resident
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    status = _lib.read_device_status(wsf)
+    if status != 0:
+        raise RuntimeError(f"forward kernel reported device status {status:#x}")
+    step_ev = [(ev(), ev()) for _ in range(args.steps)]
+    kern_ev = [(ev(), ev()) for _ in range(args.steps)]
+    sampler = ClockSampler(dev)
+    barrier()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            step_ev[i][0].record(stream)
+            step(*kern_ev[i])
+            step_ev[i][1].record(stream)
+        barrier()
+    step_ms = sum(a.elapsed_time(bb) for a, bb in step_ev) / args.steps
+    kern_ms = sum(a.elapsed_time(bb) for a, bb in kern_ev) / args.steps
+    step_ms = max_over_ranks(step_ms)
+    kern_ms_max = max_over_ranks(kern_ms)
+    launches_per_step = 2 + (4 if bd is not None else 3)
+
+    # ---------------------------------------------------------------- end to end
+    head = SpartonHead(V, D, use_bias=c["bias"], process_group=group).to(dev, c["dtype"])
+    head.load({"weight": W, "bias": b} if b is not None else {"weight": W})
+    H_pin, m_pin, g_pin = H.pin_memory(), mask.pin_memory(), gs.pin_memory()
+    reps_host = torch.empty(B, Vs, dtype=c["dtype"]).pin_memory()
+    h2d = H_pin.numel() * H_pin.element_size() + m_pin.numel() * 8 + g_pin.numel() * g_pin.element_size()
+    d2h = reps_host.numel() * reps_host.element_size()
+
+    def e2e_step():
+        hid = H_pin.to(dev, non_blocking=True).requires_grad_(True)
+        msk = m_pin.to(dev, non_blocking=True)
+        gg = g_pin.to(dev, non_blocking=True)
+        out = head(hid, msk)
+        out.backward(gg)
+        reps_host.copy_(out.detach(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        e2e_step()
+    e2e_ev = [(ev(), ev()) for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_ev[i][0].record(stream)
+        e2e_step()
+        e2e_ev[i][1].record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(bb) for a, bb in e2e_ev) / args.steps)
+
+    # ---------------------------------------------------------------- report
+    peaks, peaks_src = load_peaks()
+    fl = nominal_flops(c)
+    value = fl / (step_ms * 1e-3) / 1e12
+    alg_fwd = 2.0 * D * Vs * T  # this rank's forward launch
+    achieved = alg_fwd / (kern_ms * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    traffic = profile_traffic() if world == 1 else None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config 2 distributions)",
+        "config": {"workload": "config 2: B=128 S=256 D=768 V=30522 bf16, lengths U[32,256], bias",
+                   "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
+                   "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "tokens_per_s": round(B * S / (step_ms * 1e-3), 1),
+        "valid_tokens_per_s": round(T / (step_ms * 1e-3), 1),
+        "algorithmic_tflops": round((2.0 * D * V * T + 4.0 * D * B * V) / (step_ms * 1e-3) / 1e12, 2),
+        "frac_of_bf16_peak_nominal": round(value / peak, 4),
+        "fwd_kernel_ms": round(kern_ms_max, 4),
+        "roofline": {"kernel": "fwd_tc_kernel", "bound": "tensor", "achieved": round(achieved, 2),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "frac_of_sustained": round(achieved / float(peaks["bf16_tflops_sustained"]), 4),
+                     "peak_source": f"{peaks_src} bf16_tflops (burst)",
+                     "algorithmic_flops_per_launch": alg_fwd, "traffic": traffic},
+        "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "SpartonHead forward + autograd backward, pinned host inputs"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            res = cpu_baseline(c, args.cpu_rows, steps=3, warmup=1)
+            line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as e:  # pragma: no cover
+            line["cpu_baseline"] = {"error": repr(e)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(group=group, device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

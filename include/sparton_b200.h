@@ -1,0 +1,161 @@
+/*
+ * sparton_b200.h — C ABI of the B200-native SPLADE projection head.
+ *
+ * The head computes, for hidden states H[B,S,D], decoder weight W[V,D],
+ * optional bias b[V] and attention mask M[B,S]:
+ *
+ *     logits[b,s,v] = H[b,s,:] . W[v,:] + b[v]
+ *     reps[b,v]     = max_s log1p(relu(logits[b,s,v] * M[b,s]))
+ *     idx[b,v]      = smallest s attaining that max (0 when the max is <= 0)
+ *
+ * and its backward (g = dLoss/dreps):
+ *
+ *     g'[b,v]            = reps[b,v] > 0 ? g[b,v] * exp(-reps[b,v]) : 0
+ *     dH[b,idx[b,v],:]  += g'[b,v] * W[v,:]
+ *     dW[v,:]            = sum_b g'[b,v] * H[b,idx[b,v],:]
+ *     db[v]              = sum_b g'[b,v]
+ *
+ * Upstream, the same operator is the pair of torch custom ops
+ * `sparton::fused_sparton_fwd` / `sparton::fused_sparton_bwd`
+ * (hhkbble/sparton src/sparton/sparton_kernel.py:643-707), whose host drivers
+ * are fused_sparton_fwd_with_indices (:226-253) and
+ * fused_sparton_bwd_with_bias (:567-597). Those are Python functions bound
+ * to torch tensors; this header is the language-neutral boundary that replaces
+ * them: plain device pointers, sizes and a CUDA stream.
+ *
+ * Conventions for every entry point:
+ *  - All tensors are dense, row-major (C-contiguous) device memory.
+ *  - The library never allocates, frees or synchronises. The caller owns all
+ *    buffers, including the scratch `workspace`, whose size is given by the
+ *    matching *_workspace_size() function. Workspace pointers must be 256-byte
+ *    aligned (any cudaMalloc / torch allocation is).
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Kernels are
+ *    enqueued on it; the call returns before they finish.
+ *  - Return value: SPARTON_OK (0) or a sparton_status code; on error nothing
+ *    was launched and sparton_last_error() describes the problem. The message
+ *    is thread-local.
+ *  - Device-side waits are bounded. A kernel that gives up records a nonzero
+ *    code in the workspace; sparton_read_device_status() returns it.
+ */
+#ifndef SPARTON_B200_H_
+#define SPARTON_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPARTON_ABI_VERSION 1
+
+typedef enum {
+  SPARTON_OK = 0,
+  SPARTON_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer, misaligned buffer */
+  SPARTON_ERR_UNSUPPORTED = 2,      /* dtype / size outside what the kernels cover */
+  SPARTON_ERR_WORKSPACE = 3,        /* workspace too small */
+  SPARTON_ERR_CUDA = 4,             /* a CUDA runtime / driver call failed */
+  SPARTON_ERR_DEVICE = 5            /* no sm_100 device current */
+} sparton_status;
+
+/* Element type of hidden / weight / bias / reps (and of gradients unless F32
+ * is requested for them). */
+typedef enum {
+  SPARTON_DTYPE_F32 = 0,
+  SPARTON_DTYPE_F16 = 1,
+  SPARTON_DTYPE_BF16 = 2
+} sparton_dtype;
+
+/* Element type of the attention mask [B,S]. Any nonzero entry marks a valid
+ * token. The upstream kernel multiplies logits by the mask value
+ * (sparton_kernel.py:147); for 0/1 masks (every HF tokenizer mask) the two
+ * are identical. */
+typedef enum {
+  SPARTON_MASK_U8 = 0, /* bool / uint8 */
+  SPARTON_MASK_I32 = 1,
+  SPARTON_MASK_I64 = 2,
+  SPARTON_MASK_F32 = 3,
+  SPARTON_MASK_F16 = 4,
+  SPARTON_MASK_BF16 = 5
+} sparton_mask_dtype;
+
+/* Device status codes written by kernels into the workspace header. */
+#define SPARTON_DEV_OK 0u
+#define SPARTON_DEV_TIMEOUT_PRODUCER 0x101u
+#define SPARTON_DEV_TIMEOUT_MMA 0x102u
+#define SPARTON_DEV_TIMEOUT_EPILOGUE 0x103u
+#define SPARTON_DEV_TIMEOUT_DRAIN 0x104u
+
+int sparton_abi_version(void);
+
+/* Human-readable description of the last error returned on this thread. */
+const char* sparton_last_error(void);
+
+/* ---------------------------------------------------------------- forward */
+
+/* Bytes of workspace sparton_fwd / sparton_mask_prepare need. */
+size_t sparton_fwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V);
+
+/* Full forward. Replaces fused_sparton_fwd_with_indices
+ * (sparton_kernel.py:226-253) and the custom op sparton::fused_sparton_fwd
+ * (:643-652).
+ *   hidden [B,S,D], weight [V,D], bias [V] (NULL = no bias), all `dtype`
+ *   mask   [B,S] of `mask_dtype`
+ *   reps   [B,V] `dtype` (out), idx [B,V] int32 (out; upstream uses int64)
+ * bf16 / f16 run on tcgen05 tensor cores with fp32 accumulation; f32 runs an
+ * exact fp32 FMA path. Launches sparton_mask_prepare + sparton_fwd_prepared. */
+int sparton_fwd(const void* hidden, const void* weight, const void* bias,
+                const void* mask, int mask_dtype, int dtype,
+                int64_t B, int64_t S, int64_t D, int64_t V,
+                void* reps, int32_t* idx,
+                void* workspace, size_t workspace_size, void* stream);
+
+/* First half of sparton_fwd: reduce the mask to per-row bit words and
+ * per-row extents (last valid position + 1) in the workspace, and reset the
+ * device status and tile counter. Upstream re-reads the mask inside its
+ * reduce kernel (sparton_kernel.py:140-147). */
+int sparton_mask_prepare(const void* mask, int mask_dtype, int64_t B, int64_t S,
+                         void* workspace, size_t workspace_size, void* stream);
+
+/* Second half of sparton_fwd: the fused GEMM + masked max/argmax + log1p
+ * kernel, given a workspace filled by sparton_mask_prepare for the same B, S.
+ * Replaces the per-chunk matmul_bias + reduce loop of
+ * fused_sparton_fwd_with_indices (sparton_kernel.py:240-251). */
+int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bias,
+                         int dtype, int64_t B, int64_t S, int64_t D, int64_t V,
+                         void* reps, int32_t* idx,
+                         void* workspace, size_t workspace_size, void* stream);
+
+/* --------------------------------------------------------------- backward */
+
+/* Bytes of workspace sparton_bwd needs. */
+size_t sparton_bwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V);
+
+/* Backward. Replaces fused_sparton_bwd_with_bias (sparton_kernel.py:567-597)
+ * and the custom op sparton::fused_sparton_bwd (:663-685).
+ *   grad_reps [B,V], reps [B,V] (`dtype`), idx [B,V] int32 from sparton_fwd
+ *   hidden [B,S,D], weight [V,D] (`dtype`)
+ *   d_hidden [B,S,D] (out, `d_hidden_dtype`), d_weight [V,D] and d_bias [V]
+ *   (out, `d_param_dtype`); each dtype is `dtype` or SPARTON_DTYPE_F32. Any of
+ *   the three outputs may be NULL to skip it.
+ * Every output element is written (no pre-zeroing needed); the result is
+ * deterministic (no atomics). Upstream accumulates with fp32 atomics into
+ * zero-initialised fp32 buffers. */
+int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx,
+                const void* hidden, const void* weight, int dtype,
+                int64_t B, int64_t S, int64_t D, int64_t V,
+                void* d_hidden, void* d_weight, void* d_bias,
+                int d_hidden_dtype, int d_param_dtype,
+                void* workspace, size_t workspace_size, void* stream);
+
+/* --------------------------------------------------------------- status */
+
+/* Copies the device status word of a workspace used by sparton_fwd /
+ * sparton_bwd to *code (synchronises `stream`). 0 = no device-side timeout. */
+int sparton_read_device_status(const void* workspace, void* stream, uint32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARTON_B200_H_ */

@@ -1,0 +1,234 @@
+// capi.cu — the extern "C" boundary declared in include/sparton_b200.h.
+// Validates every argument before anything is launched (upstream relies on
+// Python asserts: hhkbble/sparton src/sparton/sparton_kernel.py:179-182,
+// :578-580, :650, :673), carves the caller's workspace and dispatches to the
+// launchers.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "internal.h"
+
+namespace sparton {
+
+namespace {
+thread_local char g_last_error[512] = "";
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_sizes(int64_t B, int64_t S, int64_t D, int64_t V) {
+  if (B < 0 || S < 0 || D < 0 || V < 0)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "negative size (B=%lld S=%lld D=%lld V=%lld)",
+                (long long)B, (long long)S, (long long)D, (long long)V);
+  if (B > 65535 || S > (1 << 24) || D > (1 << 16) || V > (1 << 28) || B * S > (1ll << 31) - 1 ||
+      B * V > (1ll << 31) - 1)
+    return fail(SPARTON_ERR_UNSUPPORTED,
+                "sizes out of range (B=%lld S=%lld D=%lld V=%lld; need B<=65535, B*S and B*V < 2^31)",
+                (long long)B, (long long)S, (long long)D, (long long)V);
+  if (D % 8 != 0)
+    return fail(SPARTON_ERR_UNSUPPORTED, "hidden size D=%lld must be a multiple of 8", (long long)D);
+  return SPARTON_OK;
+}
+
+int check_dtype(int dtype) {
+  if (dtype != SPARTON_DTYPE_F32 && dtype != SPARTON_DTYPE_F16 && dtype != SPARTON_DTYPE_BF16)
+    return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);
+  return SPARTON_OK;
+}
+
+int check_device() {
+  if (!device_is_sm100())
+    return fail(SPARTON_ERR_DEVICE, "the current CUDA device is not compute capability 10.x (sm_100)");
+  return SPARTON_OK;
+}
+
+int check_workspace(const void* ws, size_t have, size_t need) {
+  if (ws == nullptr || have < need)
+    return fail(SPARTON_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given%s", need, have,
+                ws == nullptr ? " (NULL)" : "");
+  if (!aligned(ws, 256)) return fail(SPARTON_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  return SPARTON_OK;
+}
+
+#define SPARTON_TRY(expr)           \
+  do {                              \
+    const int st_ = (expr);         \
+    if (st_ != SPARTON_OK) return st_; \
+  } while (0)
+
+}  // namespace
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(SPARTON_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
+}
+
+namespace {
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool known = false;
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+DeviceInfo current_device_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DeviceInfo{};
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (!g_dev[dev].known) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return DeviceInfo{};
+    g_dev[dev].sms = sms;
+    g_dev[dev].major = major;
+    g_dev[dev].known = true;
+  }
+  return g_dev[dev];
+}
+}  // namespace
+
+int device_sm_count() {
+  const DeviceInfo d = current_device_info();
+  return d.sms > 0 ? d.sms : 1;
+}
+
+bool device_is_sm100() { return current_device_info().major == 10; }
+
+}  // namespace sparton
+
+using namespace sparton;
+
+extern "C" {
+
+int sparton_abi_version(void) { return SPARTON_ABI_VERSION; }
+
+const char* sparton_last_error(void) { return g_last_error; }
+
+size_t sparton_fwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V) {
+  (void)D;
+  (void)V;
+  if (B < 0 || S < 0) return 0;
+  return fwd_workspace_bytes(B, S);
+}
+
+int sparton_mask_prepare(const void* mask, int mask_dtype, int64_t B, int64_t S, void* workspace,
+                         size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_sizes(B, S, 8, 0));
+  if (mask_dtype < SPARTON_MASK_U8 || mask_dtype > SPARTON_MASK_BF16)
+    return fail(SPARTON_ERR_UNSUPPORTED, "unknown mask dtype %d", mask_dtype);
+  SPARTON_TRY(check_workspace(workspace, workspace_size, fwd_workspace_bytes(B, S)));
+  if (B == 0) return SPARTON_OK;
+  if (mask == nullptr && S > 0) return fail(SPARTON_ERR_INVALID_ARGUMENT, "mask is NULL");
+  SPARTON_TRY(check_device());
+  const FwdWorkspace ws = fwd_workspace_carve(workspace, B, S);
+  return launch_mask_prepare(mask, mask_dtype, static_cast<int>(B), static_cast<int>(S), ws,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bias, int dtype,
+                         int64_t B, int64_t S, int64_t D, int64_t V, void* reps, int32_t* idx,
+                         void* workspace, size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_sizes(B, S, D, V));
+  SPARTON_TRY(check_dtype(dtype));
+  SPARTON_TRY(check_workspace(workspace, workspace_size, fwd_workspace_bytes(B, S)));
+  if (B == 0 || V == 0) return SPARTON_OK;
+  if (reps == nullptr || idx == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps / idx output is NULL");
+  if ((S > 0 && (hidden == nullptr || D == 0)) || weight == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "hidden / weight is NULL or D == 0");
+  if (!aligned(hidden, 16) || !aligned(weight, 16))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "hidden and weight must be 16-byte aligned");
+  SPARTON_TRY(check_device());
+  const FwdWorkspace ws = fwd_workspace_carve(workspace, B, S);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int b = static_cast<int>(B), s = static_cast<int>(S), d = static_cast<int>(D),
+            v = static_cast<int>(V);
+  if (dtype == SPARTON_DTYPE_F32)
+    return launch_fwd_f32(static_cast<const float*>(hidden), static_cast<const float*>(weight),
+                          static_cast<const float*>(bias), b, s, d, v, static_cast<float*>(reps),
+                          idx, ws, st);
+  if (S == 0) {
+    // No positions at all: every output is the empty-row value (0, index 0).
+    cudaError_t e = cudaMemsetAsync(reps, 0, static_cast<size_t>(B * V) * 2, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(idx, 0, static_cast<size_t>(B * V) * 4, st);
+    return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "cudaMemsetAsync");
+  }
+  return launch_fwd_tc(dtype, hidden, weight, bias, b, s, d, v, reps, idx, ws, st);
+}
+
+int sparton_fwd(const void* hidden, const void* weight, const void* bias, const void* mask,
+                int mask_dtype, int dtype, int64_t B, int64_t S, int64_t D, int64_t V, void* reps,
+                int32_t* idx, void* workspace, size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_sizes(B, S, D, V));
+  SPARTON_TRY(check_dtype(dtype));
+  SPARTON_TRY(sparton_mask_prepare(mask, mask_dtype, B, S, workspace, workspace_size, stream));
+  return sparton_fwd_prepared(hidden, weight, bias, dtype, B, S, D, V, reps, idx, workspace,
+                              workspace_size, stream);
+}
+
+size_t sparton_bwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V) {
+  (void)D;
+  if (B < 0 || S < 0 || V < 0) return 0;
+  return bwd_workspace_bytes(B, S, V);
+}
+
+int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx, const void* hidden,
+                const void* weight, int dtype, int64_t B, int64_t S, int64_t D, int64_t V,
+                void* d_hidden, void* d_weight, void* d_bias, int d_hidden_dtype,
+                int d_param_dtype, void* workspace, size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_sizes(B, S, D, V));
+  SPARTON_TRY(check_dtype(dtype));
+  if ((d_hidden_dtype != dtype && d_hidden_dtype != SPARTON_DTYPE_F32) ||
+      (d_param_dtype != dtype && d_param_dtype != SPARTON_DTYPE_F32))
+    return fail(SPARTON_ERR_UNSUPPORTED, "gradient dtypes must equal dtype or be F32");
+  SPARTON_TRY(check_workspace(workspace, workspace_size, bwd_workspace_bytes(B, S, V)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t hsz = d_hidden_dtype == SPARTON_DTYPE_F32 ? 4 : 2;
+  const size_t psz = d_param_dtype == SPARTON_DTYPE_F32 ? 4 : 2;
+  if (B == 0 || V == 0 || S == 0) {
+    // Nothing flows back: write the zero gradients the caller asked for.
+    cudaError_t e = cudaSuccess;
+    if (d_hidden != nullptr && B * S * D > 0)
+      e = cudaMemsetAsync(d_hidden, 0, static_cast<size_t>(B * S * D) * hsz, st);
+    if (e == cudaSuccess && d_weight != nullptr && V * D > 0)
+      e = cudaMemsetAsync(d_weight, 0, static_cast<size_t>(V * D) * psz, st);
+    if (e == cudaSuccess && d_bias != nullptr && V > 0)
+      e = cudaMemsetAsync(d_bias, 0, static_cast<size_t>(V) * psz, st);
+    return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (grad_reps == nullptr || reps == nullptr || idx == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "grad_reps / reps / idx is NULL");
+  if ((d_hidden != nullptr && weight == nullptr) || (d_weight != nullptr && hidden == nullptr))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "hidden / weight is NULL");
+  if (D == 0) return fail(SPARTON_ERR_INVALID_ARGUMENT, "D == 0");
+  const void* ptrs[5] = {hidden, weight, d_hidden, d_weight, nullptr};
+  for (const void* p : ptrs)
+    if (p != nullptr && !aligned(p, 16))
+      return fail(SPARTON_ERR_INVALID_ARGUMENT, "hidden / weight / gradients must be 16-byte aligned");
+  SPARTON_TRY(check_device());
+  const BwdWorkspace ws = bwd_workspace_carve(workspace, B, S, V);
+  return launch_bwd(dtype, grad_reps, reps, idx, hidden, weight, static_cast<int>(B),
+                    static_cast<int>(S), static_cast<int>(D), static_cast<int>(V), d_hidden,
+                    d_weight, d_bias, d_hidden_dtype, d_param_dtype, ws, st);
+}
+
+int sparton_read_device_status(const void* workspace, void* stream, uint32_t* code) {
+  if (workspace == nullptr || code == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "workspace / code is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(code, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "reading device status");
+}
+
+}  // extern "C"

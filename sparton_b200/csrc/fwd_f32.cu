@@ -1,0 +1,114 @@
+// fwd_f32.cu — forward for fp32 inputs. tcgen05 has no fp32-exact MMA kind
+// (kind::tf32 keeps 10 mantissa bits), and fp32 parity is required at rtol
+// 1e-5, so fp32 runs a CUDA-core FMA kernel with the same fused epilogue as the
+// tensor-core path: masked max / first argmax over positions (upstream
+// hhkbble/sparton src/sparton/sparton_kernel.py:112-156), bias, relu, log1p
+// (:158-161). fp32 is the reference's CPU configuration; the bf16 / f16 path is
+// the performance path.
+//
+// Tile: 64 vocab ids x 64 positions per step, K in chunks of 32, 256 threads,
+// 4x4 outputs per thread accumulated with fmaf in increasing k. Each CTA owns
+// (vocab tile, batch row) and walks the positions up to the row's extent.
+#include <math.h>
+
+#include "internal.h"
+
+namespace sparton {
+namespace {
+
+constexpr int kTV = 64, kTS = 64, kTK = 32;
+
+__global__ void __launch_bounds__(256)
+    fwd_f32_kernel(const float* __restrict__ H, const float* __restrict__ W,
+                   const float* __restrict__ bias, int S, int D, int V, float* __restrict__ reps,
+                   int32_t* __restrict__ idx, const uint32_t* __restrict__ bits, int S32,
+                   const int* __restrict__ extent) {
+  __shared__ float As[kTK][kTV + 4];
+  __shared__ float Bs[kTK][kTS + 4];
+  __shared__ float Cs[kTV][kTS + 1];
+  const int v0 = blockIdx.x * kTV;
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int tv = tid >> 4, ts = tid & 15;
+  const int E = extent[b];
+  const float* Hb = H + static_cast<size_t>(b) * S * D;
+  const uint32_t* brow = bits + static_cast<size_t>(b) * S32;
+  float best = -INFINITY;
+  int best_idx = 0;
+  for (int s0 = 0; s0 < E; s0 += kTS) {
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < D; k0 += kTK) {
+      for (int e = tid; e < kTV * kTK; e += 256) {
+        const int i = e / kTK, kk = e % kTK;
+        const int v = v0 + i, k = k0 + kk;
+        As[kk][i] = (v < V && k < D) ? W[static_cast<size_t>(v) * D + k] : 0.f;
+      }
+      for (int e = tid; e < kTS * kTK; e += 256) {
+        const int i = e / kTK, kk = e % kTK;
+        const int s = s0 + i, k = k0 + kk;
+        Bs[kk][i] = (s < S && k < D) ? Hb[static_cast<size_t>(s) * D + k] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int kk = 0; kk < kTK; ++kk) {
+        float a[4], c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = As[kk][tv * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[j] = Bs[kk][ts * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], c[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Cs[tv * 4 + i][ts * 4 + j] = acc[i][j];
+    __syncthreads();
+    if (tid < kTV) {
+      const int n = min(kTS, E - s0);
+      for (int cidx = 0; cidx < n; ++cidx) {
+        const int s = s0 + cidx;
+        if (!((brow[s >> 5] >> (s & 31)) & 1u)) continue;
+        const float x = Cs[tid][cidx];
+        if (x > best) {
+          best = x;
+          best_idx = s;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (tid < kTV) {
+    const int v = v0 + tid;
+    if (v < V) {
+      const float logit = best + (bias != nullptr ? bias[v] : 0.f);
+      const bool pos = logit > 0.f;
+      const size_t o = static_cast<size_t>(b) * V + v;
+      reps[o] = pos ? log1pf(logit) : 0.f;
+      idx[o] = pos ? best_idx : 0;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_fwd_f32(const float* hidden, const float* weight, const float* bias, int B, int S,
+                   int D, int V, float* reps, int32_t* idx, const FwdWorkspace& ws,
+                   cudaStream_t stream) {
+  const dim3 grid((V + kTV - 1) / kTV, B);
+  fwd_f32_kernel<<<grid, 256, 0, stream>>>(hidden, weight, bias, S, D, V, reps, idx, ws.bits,
+                                           ws.S32, ws.extent);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fwd_f32_kernel launch");
+  return SPARTON_OK;
+}
+
+}  // namespace sparton

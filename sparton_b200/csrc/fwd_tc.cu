@@ -1,0 +1,529 @@
+// fwd_tc.cu — K1: the fused SPLADE head forward on sm_100a tensor cores.
+//
+// What it replaces upstream (hhkbble/sparton src/sparton/sparton_kernel.py):
+//   fused_sparton_fwd_with_indices :226-253 loops over vocab chunks; per chunk
+//   a torch.compile GEMM (+bias) writes logits [B,S,C] to HBM (:244-247) and the
+//   Triton kernel reduce_seq_max_log1p_relu_kernel_with_indices (:84-168)
+//   re-reads them for the masked max / argmax over S and log1p(relu(.)).
+// Here one persistent kernel does all of it and [B,S,V] never exists.
+//
+// Orientation. The GEMM is computed transposed: the MMA's M dimension is the
+// vocabulary (128 rows of W per tile, one TMEM lane per vocab id) and N is the
+// token dimension (up to 256 positions of one batch row). A thread of the
+// epilogue therefore owns one vocab id and scans its own TMEM lane along the
+// sequence: the max / argmax over S needs no cross-thread reduction.
+//
+// Work unit = (vocab tile of 128, batch row b). The unit covers positions
+// [0, E_b) in s-tiles of <= 256, where E_b is the last valid position + 1;
+// the MMA N of the last s-tile is rounded up to 16 only, so padded positions
+// beyond E_b cost nothing. Units are handed out by an atomic counter
+// (dynamic persistent scheduling), in panel order: panels of `panel_b` batch
+// rows whose hidden states fit in L2, vocab-tile-major inside a panel.
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0    TMA producer: W tile [128 x 64] + hidden tile [<=256 x 64] per
+//             stage, 4 stages, 128-byte swizzle.
+//   warp 1    TMEM owner + MMA issuer: tcgen05.mma kind::f16, fp32 accumulator
+//             in TMEM, two 256-column accumulators (MMA of the next s-tile
+//             overlaps the epilogue of the previous one).
+//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time, masked running max and
+//             first-index argmax over positions (strict >, as upstream
+//             :150-156), then bias, relu, log1p and the stores of reps / idx.
+//
+// Every wait is bounded (ptx.cuh); on timeout the CTA records a status code,
+// drains its in-flight TMA copies and MMAs, frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <math.h>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sparton {
+namespace {
+
+constexpr int kBM = 128;        // vocab rows per tile = MMA M = TMEM lanes
+constexpr int kBN = 256;        // max positions per s-tile = MMA N
+constexpr int kBK = 64;         // K elements per stage: 128-byte rows
+constexpr int kStages = 4;      // TMA -> MMA pipeline depth
+constexpr int kBoxRows = 64;    // hidden rows per TMA box
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kBBytes = kBN * kBK * 2;
+constexpr int kBoxBytes = kBoxRows * kBK * 2;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kSchedSlots = 4;  // unit ids in flight between roles
+constexpr int kNumAcc = 2;
+constexpr int kTmemCols = kNumAcc * kBN;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+
+// Barrier indices inside the barrier block.
+constexpr int kBarFull = 0;
+constexpr int kBarEmpty = kBarFull + kStages;
+constexpr int kBarTFull = kBarEmpty + kStages;
+constexpr int kBarTEmpty = kBarTFull + kNumAcc;
+constexpr int kBarSFull = kBarTEmpty + kNumAcc;
+constexpr int kBarSEmpty = kBarSFull + kSchedSlots;
+constexpr int kBarDrain = kBarSEmpty + kSchedSlots;
+constexpr int kNumBars = kBarDrain + 1;
+
+constexpr int kCtrlOffset = kStages * kStageBytes;         // barriers + slots
+constexpr int kSlotOffset = kCtrlOffset + kNumBars * 8;    // long long[kSchedSlots]
+constexpr int kTmemHolderOffset = kSlotOffset + kSchedSlots * 8;
+constexpr int kAbortOffset = kTmemHolderOffset + 4;
+constexpr int kCtrlBytes = 512;
+static_assert(kAbortOffset + 4 <= kCtrlOffset + kCtrlBytes, "control block overflow");
+constexpr int kSmemBytes = kCtrlOffset + kCtrlBytes + 1024;  // + alignment slack
+
+struct FwdTcParams {
+  int B, S, D, V;
+  int num_vtiles;
+  int num_kblocks;
+  int panel_b;
+  long long num_units;
+  const uint32_t* bits;
+  int S32;
+  const int* extent;
+  const void* bias;
+  void* reps;
+  int32_t* idx;
+  unsigned int* counter;  // next unit to hand out (minus gridDim.x)
+  unsigned int* done;     // CTAs finished; the last one resets both counters
+  unsigned int* status;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_float(T x);
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+template <>
+__device__ __forceinline__ float to_float<__half>(__half x) {
+  return __half2float(x);
+}
+template <typename T>
+__device__ __forceinline__ T from_float(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <>
+__device__ __forceinline__ __half from_float<__half>(float x) {
+  return __float2half_rn(x);
+}
+
+__device__ __forceinline__ void decode_unit(long long j, const FwdTcParams& p, int& vt, int& b) {
+  const long long per_panel = static_cast<long long>(p.num_vtiles) * p.panel_b;
+  const long long panel = j / per_panel;
+  const long long r = j - panel * per_panel;
+  const int b0 = static_cast<int>(panel * p.panel_b);
+  const int pb = min(p.panel_b, p.B - b0);
+  vt = static_cast<int>(r / pb);
+  b = b0 + static_cast<int>(r % pb);
+}
+
+struct Ctrl {
+  uint32_t bar0;  // shared address of barrier 0
+  long long* slots;
+  volatile int* abort_flag;
+  __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * i; }
+};
+
+__device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const CUtensorMap* tmH,
+                             uint32_t stage_base, const Ctrl& c) {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t issued_mask = 0, issued_parity = 0;
+  long long j = blockIdx.x;
+  int k = 0;
+  bool ok = true;
+  while (true) {
+    const int slot = k % kSchedSlots;
+    const uint32_t sph = (k / kSchedSlots) & 1;
+    if (!mbar_wait_bounded(c.bar(kBarSEmpty + slot), sph ^ 1, c.abort_flag, p.status,
+                           SPARTON_DEV_TIMEOUT_PRODUCER)) {
+      ok = false;
+      break;
+    }
+    const long long unit = j < p.num_units ? j : -1;
+    c.slots[slot] = unit;
+    mbar_arrive(c.bar(kBarSFull + slot));
+    ++k;
+    if (unit < 0) break;
+    const long long next = static_cast<long long>(atomicAdd(p.counter, 1u)) + gridDim.x;
+    int vt, b;
+    decode_unit(unit, p, vt, b);
+    const int E = p.extent[b];
+    for (int s0 = 0; s0 < E && ok; s0 += kBN) {
+      const int ncols = min(kBN, E - s0);
+      const int nbox = (ncols + kBoxRows - 1) / kBoxRows;
+      const uint32_t bytes = kABytes + nbox * kBoxBytes;
+      const int row0 = b * p.S + s0;
+      for (int kb = 0; kb < p.num_kblocks; ++kb) {
+        if (!mbar_wait_bounded(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
+                               SPARTON_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = c.bar(kBarFull + stage);
+        mbar_arrive_expect_tx(full, bytes);
+        const uint32_t a_dst = stage_base + stage * kStageBytes;
+        tma_load_2d(a_dst, tmW, full, kb * kBK, vt * kBM);
+        for (int i = 0; i < nbox; ++i)
+          tma_load_2d(a_dst + kABytes + i * kBoxBytes, tmH, full, kb * kBK, row0 + i * kBoxRows);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (!ok) break;
+    j = next;
+  }
+  if (!ok) {
+    // Unwinding: let every issued copy land before the CTA's shared memory goes away.
+    for (int s = 0; s < kStages; ++s)
+      if (issued_mask & (1u << s))
+        if (!mbar_wait_drain(c.bar(kBarFull + s), (issued_parity >> s) & 1))
+          atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
+  }
+}
+
+template <uint32_t kFmt>
+__device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem_base,
+                        const Ctrl& c) {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t tile = 0;
+  int k = 0;
+  bool ok = true;
+  bool issued = false;
+  while (ok) {
+    const int slot = k % kSchedSlots;
+    const uint32_t sph = (k / kSchedSlots) & 1;
+    if (!mbar_wait_bounded(c.bar(kBarSFull + slot), sph, c.abort_flag, p.status,
+                           SPARTON_DEV_TIMEOUT_MMA)) {
+      ok = false;
+      break;
+    }
+    const long long unit = c.slots[slot];
+    mbar_arrive(c.bar(kBarSEmpty + slot));
+    ++k;
+    if (unit < 0) break;
+    int vt, b;
+    decode_unit(unit, p, vt, b);
+    const int E = p.extent[b];
+    for (int s0 = 0; s0 < E; s0 += kBN) {
+      const int acc = tile & 1;
+      const uint32_t aph = (tile >> 1) & 1;
+      if (!mbar_wait_bounded(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
+                             SPARTON_DEV_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t ncols = static_cast<uint32_t>(min(kBN, E - s0));
+      const uint32_t n_mma = (ncols + 15u) & ~15u;
+      const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma);
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+      for (int kb = 0; kb < p.num_kblocks; ++kb) {
+        if (!mbar_wait_bounded(c.bar(kBarFull + stage), phase, c.abort_flag, p.status,
+                               SPARTON_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t a_addr = stage_base + stage * kStageBytes;
+        const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          umma_f16(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
+                   idesc, (kb | kk) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(c.bar(kBarEmpty + stage));
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      umma_commit(c.bar(kBarTFull + acc));
+      ++tile;
+    }
+  }
+  if (!ok && issued) {
+    // Unwinding: wait for every MMA this thread issued before TMEM is freed.
+    umma_commit(c.bar(kBarDrain));
+    if (!mbar_wait_drain(c.bar(kBarDrain), 0)) atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
+  }
+}
+
+template <typename T>
+__device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
+                             int lane) {
+  const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
+  const int row = quad * 32 + lane;
+  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+  uint32_t tile = 0;
+  int k = 0;
+  while (true) {
+    const int slot = k % kSchedSlots;
+    const uint32_t sph = (k / kSchedSlots) & 1;
+    if (!mbar_wait_bounded(c.bar(kBarSFull + slot), sph, c.abort_flag, p.status,
+                           SPARTON_DEV_TIMEOUT_EPILOGUE))
+      break;
+    const long long unit = c.slots[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(c.bar(kBarSEmpty + slot));
+    ++k;
+    if (unit < 0) break;
+    int vt, b;
+    decode_unit(unit, p, vt, b);
+    const int E = p.extent[b];
+    const uint32_t* bits_row = p.bits + static_cast<size_t>(b) * p.S32;
+    float best = -INFINITY;
+    int best_idx = 0;
+    bool ok = true;
+    for (int s0 = 0; s0 < E; s0 += kBN) {
+      const int acc = tile & 1;
+      const uint32_t aph = (tile >> 1) & 1;
+      if (!mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
+                             SPARTON_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const int ncols = min(kBN, E - s0);
+      const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * kBN);
+      for (int c0 = 0; c0 < ncols; c0 += 32) {
+        const uint32_t mw = __ldg(bits_row + ((s0 + c0) >> 5));
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c0), r);
+        tmem_ld_wait();
+        if (mw == 0u) continue;
+        float cm = -INFINITY;
+        if (mw == 0xFFFFFFFFu) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) cm = fmaxf(cm, __uint_as_float(r[q]));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q)
+            cm = ((mw >> q) & 1u) ? fmaxf(cm, __uint_as_float(r[q])) : cm;
+        }
+        if (cm > best) {
+          int first = 31;
+#pragma unroll
+          for (int q = 31; q >= 0; --q)
+            if (((mw >> q) & 1u) && __uint_as_float(r[q]) == cm) first = q;
+          best = cm;
+          best_idx = s0 + c0 + first;
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(c.bar(kBarTEmpty + acc));
+      ++tile;
+    }
+    if (!ok) break;
+    const int v = vt * kBM + row;
+    if (v < p.V) {
+      // max_s(x_s + bias) = max_s(x_s) + bias: the bias is added once, after the
+      // max. Upstream's initial value 0 (:112) is the `logit > 0` test.
+      const float bias = p.bias != nullptr ? to_float<T>(static_cast<const T*>(p.bias)[v]) : 0.f;
+      const float logit = best + bias;
+      const bool pos = logit > 0.f;
+      const size_t o = static_cast<size_t>(b) * p.V + v;
+      static_cast<T*>(p.reps)[o] = from_float<T>(pos ? log1pf(logit) : 0.f);
+      p.idx[o] = pos ? best_idx : 0;
+    }
+  }
+}
+
+template <typename T, uint32_t kFmt>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
+                  const FwdTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t stage_base = smem_addr(smem);
+  Ctrl c;
+  c.bar0 = stage_base + kCtrlOffset;
+  c.slots = reinterpret_cast<long long*>(smem + kSlotOffset);
+  c.abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOffset);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kTmemHolderOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(c.bar(kBarFull + s), 1);
+      mbar_init(c.bar(kBarEmpty + s), 1);
+    }
+    for (int a = 0; a < kNumAcc; ++a) {
+      mbar_init(c.bar(kBarTFull + a), 1);
+      mbar_init(c.bar(kBarTEmpty + a), kEpiWarps);
+    }
+    for (int s = 0; s < kSchedSlots; ++s) {
+      mbar_init(c.bar(kBarSFull + s), 1);
+      mbar_init(c.bar(kBarSEmpty + s), 1 + kEpiWarps);
+    }
+    mbar_init(c.bar(kBarDrain), 1);
+    *c.abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmH);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) run_producer(p, &tmW, &tmH, stage_base, c);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) run_mma<kFmt>(p, stage_base, tmem_base, c);
+    __syncwarp();
+  } else {
+    run_epilogue<T>(p, tmem_base, c, warp, lane);
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    // Leave the scheduler counters at zero so the same prepared workspace can
+    // be launched again.
+    __threadfence();
+    if (atomicAdd(p.done, 1u) == gridDim.x - 1) {
+      atomicExch(p.counter, 0u);
+      atomicExch(p.done, 0u);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(SPARTON_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SPARTON_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return SPARTON_OK;
+}
+
+template <typename T, uint32_t kFmt>
+int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight, const void* bias,
+                 int B, int S, int D, int V, void* reps, int32_t* idx, const FwdWorkspace& ws,
+                 cudaStream_t stream) {
+  CUtensorMap tmW, tmH;
+  int st = make_map_2d(&tmW, dt, weight, static_cast<uint64_t>(D), static_cast<uint64_t>(V), kBK,
+                       kBM);
+  if (st != SPARTON_OK) return st;
+  st = make_map_2d(&tmH, dt, hidden, static_cast<uint64_t>(D),
+                   static_cast<uint64_t>(B) * static_cast<uint64_t>(S), kBK, kBoxRows);
+  if (st != SPARTON_OK) return st;
+
+  FwdTcParams p;
+  p.B = B;
+  p.S = S;
+  p.D = D;
+  p.V = V;
+  p.num_vtiles = (V + kBM - 1) / kBM;
+  p.num_kblocks = (D + kBK - 1) / kBK;
+  // Panel of batch rows whose hidden states (S*D*2 bytes each) fit in ~48 MB of L2.
+  const long long row_bytes = static_cast<long long>(S) * D * 2;
+  long long pb = (48ll << 20) / (row_bytes > 0 ? row_bytes : 1);
+  if (pb < 1) pb = 1;
+  if (pb > B) pb = B;
+  p.panel_b = static_cast<int>(pb);
+  p.num_units = static_cast<long long>(p.num_vtiles) * B;
+  p.bits = ws.bits;
+  p.S32 = ws.S32;
+  p.extent = ws.extent;
+  p.bias = bias;
+  p.reps = reps;
+  p.idx = idx;
+  p.counter = ws.counter;
+  p.done = ws.done;
+  p.status = ws.status;
+
+  static std::mutex mu;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !attr_done[dev]) {
+      e = cudaFuncSetAttribute(fwd_tc_kernel<T, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd_tc_kernel)");
+      attr_done[dev] = true;
+    }
+  }
+  const long long grid_ll = p.num_units < device_sm_count() ? p.num_units : device_sm_count();
+  const unsigned grid = static_cast<unsigned>(grid_ll > 0 ? grid_ll : 1);
+  fwd_tc_kernel<T, kFmt><<<grid, kThreads, kSmemBytes, stream>>>(tmW, tmH, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fwd_tc_kernel launch");
+  return SPARTON_OK;
+}
+
+}  // namespace
+
+int launch_fwd_tc(int dtype, const void* hidden, const void* weight, const void* bias, int B,
+                  int S, int D, int V, void* reps, int32_t* idx, const FwdWorkspace& ws,
+                  cudaStream_t stream) {
+  if (dtype == SPARTON_DTYPE_BF16)
+    return launch_typed<__nv_bfloat16, 1u>(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, hidden, weight, bias, B,
+                                           S, D, V, reps, idx, ws, stream);
+  if (dtype == SPARTON_DTYPE_F16)
+    return launch_typed<__half, 0u>(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hidden, weight, bias, B, S, D,
+                                    V, reps, idx, ws, stream);
+  return fail(SPARTON_ERR_UNSUPPORTED, "tensor-core forward supports bf16 and f16 only");
+}
+
+}  // namespace sparton

@@ -1,0 +1,109 @@
+// internal.h — declarations shared by the CUDA translation units of the
+// library: workspace layouts, launchers and error reporting. Not installed.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/sparton_b200.h"
+
+namespace sparton {
+
+// Records a printf-style message as this thread's last error and returns
+// `status` so call sites can `return fail(...)`.
+int fail(int status, const char* fmt, ...);
+
+// Turns a CUDA error into SPARTON_ERR_CUDA with a message naming `what`.
+int cuda_fail(cudaError_t err, const char* what);
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Number of SMs on the current device (cached per device).
+int device_sm_count();
+
+// True when the current device is compute capability 10.x (B200 / sm_100).
+bool device_is_sm100();
+
+// ------------------------------------------------------------ forward workspace
+// [0,256)      header: u32 status, u32 tile counter, u32 finished-CTA counter
+// extents      B x int32      last valid position + 1 of each row (0 = empty)
+// bits         B x S32 x u32  validity bit of every position, S32 = ceil(S/32)
+struct FwdWorkspace {
+  unsigned int* status;
+  unsigned int* counter;
+  unsigned int* done;
+  int* extent;
+  uint32_t* bits;
+  int S32;
+};
+
+inline size_t fwd_workspace_bytes(int64_t B, int64_t S) {
+  const int64_t S32 = (S + 31) / 32;
+  return 256 + align256(static_cast<size_t>(B) * 4) + align256(static_cast<size_t>(B * S32) * 4);
+}
+
+inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
+  FwdWorkspace w;
+  char* base = static_cast<char*>(ws);
+  w.status = reinterpret_cast<unsigned int*>(base);
+  w.counter = reinterpret_cast<unsigned int*>(base) + 1;
+  w.done = reinterpret_cast<unsigned int*>(base) + 2;
+  w.extent = reinterpret_cast<int*>(base + 256);
+  w.bits = reinterpret_cast<uint32_t*>(base + 256 + align256(static_cast<size_t>(B) * 4));
+  w.S32 = static_cast<int>((S + 31) / 32);
+  return w;
+}
+
+// ----------------------------------------------------------- backward workspace
+// [0,256)      header: u32 status
+// offs         B x (S+1) int32   bucket start of every position (CSR by position)
+// perm         B x V int32       vocab ids grouped by argmax position
+// gperm        B x V float       g' of those entries, same order
+struct BwdWorkspace {
+  unsigned int* status;
+  int* offs;
+  int* perm;
+  float* gperm;
+};
+
+inline size_t bwd_workspace_bytes(int64_t B, int64_t S, int64_t V) {
+  return 256 + align256(static_cast<size_t>(B * (S + 1)) * 4) +
+         align256(static_cast<size_t>(B * V) * 4) + align256(static_cast<size_t>(B * V) * 4);
+}
+
+inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t V) {
+  BwdWorkspace w;
+  char* base = static_cast<char*>(ws);
+  w.status = reinterpret_cast<unsigned int*>(base);
+  size_t off = 256;
+  w.offs = reinterpret_cast<int*>(base + off);
+  off += align256(static_cast<size_t>(B * (S + 1)) * 4);
+  w.perm = reinterpret_cast<int*>(base + off);
+  off += align256(static_cast<size_t>(B * V) * 4);
+  w.gperm = reinterpret_cast<float*>(base + off);
+  return w;
+}
+
+// ------------------------------------------------------------------ launchers
+// Each returns SPARTON_OK or a status after recording a message.
+
+int launch_mask_prepare(const void* mask, int mask_dtype, int B, int S, const FwdWorkspace& ws,
+                        cudaStream_t stream);
+
+// bf16 / f16: tcgen05 + TMA persistent kernel.
+int launch_fwd_tc(int dtype, const void* hidden, const void* weight, const void* bias, int B,
+                  int S, int D, int V, void* reps, int32_t* idx, const FwdWorkspace& ws,
+                  cudaStream_t stream);
+
+// f32: exact fp32 FMA kernel.
+int launch_fwd_f32(const float* hidden, const float* weight, const float* bias, int B, int S,
+                   int D, int V, float* reps, int32_t* idx, const FwdWorkspace& ws,
+                   cudaStream_t stream);
+
+int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
+               const void* hidden, const void* weight, int B, int S, int D, int V,
+               void* d_hidden, void* d_weight, void* d_bias, int d_hidden_dtype,
+               int d_param_dtype, const BwdWorkspace& ws, cudaStream_t stream);
+
+}  // namespace sparton

@@ -1,0 +1,185 @@
+"""``SpartonHead``: drop-in for hhkbble/sparton's module
+(src/sparton/sparton_kernel.py:710-746).
+
+Same constructor ``SpartonHead(vocab_size, hidden_dim, use_bias=False)``, same
+``tie_weights(decoder)``, ``load(weights_dict)``, ``init_parameters()`` and
+``forward(hidden_states, attention_mask) -> reps[B, V]``.
+
+Keyword-only additions (defaults keep the upstream behaviour):
+
+* ``process_group``: shard the vocabulary over the ranks of a
+  ``torch.distributed`` group (NCCL on GPUs). Rank r owns rows
+  ``[r*V_s, min(V, (r+1)*V_s))`` of the decoder, ``V_s = ceil(V/n)`` rounded up to
+  the kernel's 128-row vocab tile. The forward needs no communication and
+  returns ``reps[:, shard]``; the backward all-reduces (sum) the partial
+  d_hidden of every rank, in fp32 by default.
+* ``gather_output``: with a process group, all-gather the shards so forward
+  returns the full ``reps[B, V]``.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import ops
+
+VOCAB_TILE = 128
+
+
+class VocabShard:
+    """Contiguous vocabulary range owned by one rank."""
+
+    def __init__(self, vocab_size: int, world_size: int, rank: int):
+        if world_size < 1 or not 0 <= rank < world_size:
+            raise ValueError(f"bad shard spec: world_size={world_size} rank={rank}")
+        self.vocab_size = vocab_size
+        self.world_size = world_size
+        self.rank = rank
+        per = -(-vocab_size // world_size)
+        self.padded = -(-per // VOCAB_TILE) * VOCAB_TILE if world_size > 1 else vocab_size
+        self.start = min(vocab_size, rank * self.padded)
+        self.stop = min(vocab_size, self.start + self.padded)
+
+    @property
+    def size(self) -> int:
+        return self.stop - self.start
+
+    def __repr__(self) -> str:
+        return (f"VocabShard(rank={self.rank}/{self.world_size}, "
+                f"rows=[{self.start},{self.stop}) of {self.vocab_size})")
+
+
+class _ShardedHead(torch.autograd.Function):
+    """Vocab-sharded head: local fused forward; backward = local gradients plus an
+    all-reduce (sum) of the partial d_hidden over the group."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, bias, mask, group, reduce_dtype):
+        reps, idx = ops.forward_impl(hidden, weight, bias, mask)
+        ctx.save_for_backward(reps, idx, hidden, weight)
+        ctx.has_bias = bias is not None
+        ctx.group = group
+        ctx.reduce_dtype = reduce_dtype
+        return reps
+
+    @staticmethod
+    def backward(ctx, grad_reps):
+        reps, idx, hidden, weight = ctx.saved_tensors
+        need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        need_b = ctx.has_bias and ctx.needs_input_grad[2]
+        d_hidden, d_weight, d_bias = ops.backward_impl(
+            grad_reps, reps, idx, hidden, weight, need_b, need_hidden=True, need_embed=need_w,
+            hidden_grad_dtype=ctx.reduce_dtype)
+        # Every rank takes part in the all-reduce, whether or not it needs d_hidden.
+        dist.all_reduce(d_hidden, op=dist.ReduceOp.SUM, group=ctx.group)
+        return (d_hidden if need_h else None, d_weight if need_w else None,
+                d_bias if need_b else None, None, None, None)
+
+
+class _GatherVocab(torch.autograd.Function):
+    """All-gather of vocab shards [B, V_s] -> [B, V]; backward keeps the local slice."""
+
+    @staticmethod
+    def forward(ctx, local, shard: VocabShard, group):
+        ctx.shard = shard
+        B = local.shape[0]
+        buf = local.new_zeros((B, shard.padded))
+        buf[:, : local.shape[1]] = local
+        parts = [torch.empty_like(buf) for _ in range(shard.world_size)]
+        dist.all_gather(parts, buf.contiguous(), group=group)
+        return torch.cat(parts, dim=1)[:, : shard.vocab_size].contiguous()
+
+    @staticmethod
+    def backward(ctx, grad_full):
+        sh = ctx.shard
+        return grad_full[:, sh.start:sh.stop].contiguous(), None, None
+
+
+class SpartonHead(nn.Module):
+    """SPLADE head: ``reps[b,v] = max_s log1p(relu((h[b,s]·W[v] + bias[v]) * mask[b,s]))``
+    computed by one fused sm_100a kernel (no [B,S,V] logits), with an
+    atomic-free fused backward."""
+
+    def __init__(self, vocab_size, hidden_dim, use_bias=False, *,
+                 process_group: Optional[dist.ProcessGroup] = None, gather_output: bool = False,
+                 grad_reduce_dtype: torch.dtype = torch.float32):
+        super().__init__()
+        self.vocab_size = int(vocab_size)
+        self.hidden_dim = int(hidden_dim)
+        self.process_group = process_group
+        self.gather_output = gather_output
+        self.grad_reduce_dtype = grad_reduce_dtype
+        if process_group is not None:
+            world, rank = dist.get_world_size(process_group), dist.get_rank(process_group)
+        else:
+            world, rank = 1, 0
+        self.shard = VocabShard(self.vocab_size, world, rank)
+        self.weight = nn.Parameter(torch.empty(self.shard.size, self.hidden_dim))
+        if use_bias:
+            self.bias = nn.Parameter(torch.empty(self.shard.size))
+        else:
+            self.register_parameter("bias", None)
+        self.init_parameters()
+
+    @property
+    def sharded(self) -> bool:
+        return self.shard.world_size > 1
+
+    def tie_weights(self, decoder):
+        """Alias the decoder's Parameters (upstream :721-723). With a process
+        group the full Parameters are kept and each rank uses its row range, so
+        their .grad is full-size with zeros outside the shard."""
+        self.weight = decoder.weight
+        self.bias = decoder.bias
+
+    def load(self, weights_dict):
+        """Copy ``weights_dict["weight"]`` (and ``["bias"]``) in place (upstream
+        :725-734). Full [V, D] tensors are narrowed to this rank's shard."""
+        with torch.no_grad():
+            self.weight.copy_(self._rows(weights_dict["weight"], self.weight))
+            if self.bias is not None and "bias" in weights_dict:
+                self.bias.copy_(self._rows(weights_dict["bias"], self.bias))
+            else:
+                print("no bias")
+
+    def init_parameters(self):
+        """nn.Linear's initialisation (upstream :736-741)."""
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        if self.bias is not None:
+            fan_in = self.hidden_dim
+            bound = 1 / math.sqrt(fan_in) if fan_in > 0 else 0
+            nn.init.uniform_(self.bias, -bound, bound)
+
+    def _rows(self, full: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+        if self.sharded and full.shape[0] == self.vocab_size and like.shape[0] != self.vocab_size:
+            return full[self.shard.start:self.shard.stop]
+        return full
+
+    def _local_params(self):
+        w, b = self.weight, self.bias
+        if self.sharded and w.shape[0] == self.vocab_size and self.shard.size != self.vocab_size:
+            w = w.narrow(0, self.shard.start, self.shard.size)
+            b = b.narrow(0, self.shard.start, self.shard.size) if b is not None else None
+        if b is not None and b.dtype != w.dtype:
+            b = b.to(w.dtype)
+        return w, b
+
+    def forward(self, hidden_states, attention_mask):
+        weight, bias = self._local_params()
+        if not self.sharded:
+            scores, _idx = torch.ops.sparton.fused_sparton_fwd(hidden_states, weight, bias,
+                                                               attention_mask)
+            return scores
+        reps = _ShardedHead.apply(hidden_states, weight, bias, attention_mask,
+                                  self.process_group, self.grad_reduce_dtype)
+        if self.gather_output:
+            reps = _GatherVocab.apply(reps, self.shard, self.process_group)
+        return reps
+
+    def extra_repr(self) -> str:
+        return (f"vocab_size={self.vocab_size}, hidden_dim={self.hidden_dim}, "
+                f"bias={self.bias is not None}, {self.shard}")

@@ -1,0 +1,102 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point that
+include/sparton_b200.h declares, and rejects bad arguments before touching a
+GPU. No compute is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from sparton_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "sparton_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sparton_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    assert {"sparton_fwd", "sparton_bwd", "sparton_fwd_workspace_size",
+            "sparton_bwd_workspace_size", "sparton_last_error"} <= set(names)
+    assert sorted(_lib.EXPORTED_SYMBOLS) == names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version(lib):
+    assert lib.sparton_abi_version() == 1
+
+
+def test_workspace_sizes(lib):
+    B, S, D, V = 128, 256, 768, 30522
+    fw = lib.sparton_fwd_workspace_size(B, S, D, V)
+    assert fw >= 256 + 4 * B + 4 * B * (S // 32)
+    bw = lib.sparton_bwd_workspace_size(B, S, D, V)
+    assert bw >= 4 * B * (S + 1) + 8 * B * V
+    assert lib.sparton_fwd_workspace_size(-1, S, D, V) == 0
+
+
+def _fwd(lib, B=2, S=8, D=16, V=10, ws=None, ws_size=None, dtype=2, mask_dtype=2):
+    dummy = ctypes.c_void_p(0x1000)
+    wsp = ctypes.c_void_p(0x100000) if ws is None else ws
+    size = lib.sparton_fwd_workspace_size(B, S, D, V) if ws_size is None else ws_size
+    return lib.sparton_fwd(dummy, dummy, None, dummy, mask_dtype, dtype, B, S, D, V, dummy, dummy,
+                           wsp, size, None)
+
+
+def test_rejects_negative_sizes(lib):
+    assert _fwd(lib, B=-1) == _lib.ERR_INVALID_ARGUMENT
+    assert "negative" in _lib.last_error()
+
+
+def test_rejects_unaligned_hidden_size(lib):
+    assert _fwd(lib, D=12) == _lib.ERR_UNSUPPORTED
+    assert "multiple of 8" in _lib.last_error()
+
+
+def test_rejects_small_workspace(lib):
+    assert _fwd(lib, ws_size=16) == _lib.ERR_WORKSPACE
+    assert "workspace" in _lib.last_error()
+
+
+def test_rejects_unknown_dtypes(lib):
+    assert _fwd(lib, dtype=7) == _lib.ERR_UNSUPPORTED
+    assert _fwd(lib, mask_dtype=9) == _lib.ERR_UNSUPPORTED
+
+
+def test_bwd_rejects_bad_grad_dtype(lib):
+    dummy = ctypes.c_void_p(0x1000)
+    B, S, D, V = 2, 8, 16, 10
+    st = lib.sparton_bwd(dummy, dummy, dummy, dummy, dummy, 2, B, S, D, V, dummy, dummy, None,
+                         1, 2, ctypes.c_void_p(0x100000), lib.sparton_bwd_workspace_size(B, S, D, V),
+                         None)
+    assert st == _lib.ERR_UNSUPPORTED
+
+
+def test_valid_call_without_gpu_reports_device_error(lib):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert _fwd(lib) == _lib.ERR_DEVICE
+    assert "sm_100" in _lib.last_error()
+
+
+def test_check_raises_python_errors():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_INVALID_ARGUMENT, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_CUDA, "x")
+    _lib.check(_lib.OK, "x")
