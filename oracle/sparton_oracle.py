@@ -78,7 +78,8 @@ def near_tie_mask(H, W, bias, mask, rel: float = NEAR_TIE_REL):
     tol = rel * (sc + (np.abs(_f64(bias))[None, :] if bias is not None else 0.0)) + 1e-30
     zs = np.sort(zm, axis=1)
     second = zs[:, -2, :] if zm.shape[1] > 1 else np.full_like(m, -np.inf)
-    tie = (m - second) <= tol
+    with np.errstate(invalid="ignore"):  # rows with no valid position: -inf - -inf
+        tie = (m - second) <= tol
     sign = np.abs(m) <= tol
     return (tie | sign) & np.isfinite(m)
 

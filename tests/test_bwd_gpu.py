@@ -6,8 +6,11 @@ Criteria:
   indices (sparton_kernel.py:531-561): |ours - ref| <= rtol*|ref| + atol with
   rtol = 1e-2 (bf16/f16 outputs) or 1e-5 (fp32) and atol = rtol * 1e-2 * max|ref|;
 * against the torch head's own gradient (model.py:56-62 under autograd, fp64,
-  evaluated at our indices): |ours - ref| <= rtol*|ref| + rtol*rms(ref), since
-  the fused formula g*exp(-score) reads the 16-bit rounded score.
+  evaluated at our indices): |ours - ref| <= rtol*|ref| + rtol*sum|terms|, where
+  sum|terms| is the same sum taken over absolute values. The fused formula
+  g*exp(-score) reads the 16-bit rounded score (as upstream's kernel does), so
+  each term may differ from the head's g/(1+max) by up to ~rtol relative, and a
+  sum with cancellation inherits that error on its terms, not on its result.
 """
 import numpy as np
 import pytest
@@ -24,25 +27,29 @@ pytestmark = pytest.mark.gpu
 RTOL = {torch.bfloat16: 1e-2, torch.float16: 1e-2, torch.float32: 1e-5}
 
 
+def floor_of(t):
+    """Spacing of the output dtype's subnormals: the absolute rounding error a
+    stored gradient can carry whatever its relative accuracy (2^-24 for fp16)."""
+    fi = torch.finfo(t.dtype)
+    return fi.smallest_normal * fi.eps
+
+
 def close_to_kernel_oracle(ours, ref, rtol, what):
     ref = np.asarray(ref)
-    atol = rtol * 1e-2 * max(float(np.abs(ref).max()), 1e-30)
+    atol = rtol * 1e-2 * max(float(np.abs(ref).max()), 1e-30) + floor_of(ours)
     np.testing.assert_allclose(np64(ours), ref, rtol=rtol, atol=atol, err_msg=what)
 
 
 def close_to_head(ours, ref, rtol, what):
-    ref = np.asarray(ref)
-    rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
-    np.testing.assert_allclose(np64(ours), ref, rtol=rtol, atol=rtol * rms + 1e-30, err_msg=what)
+    ref, bound = ref
+    diff = np.abs(np64(ours) - ref)
+    allowed = rtol * np.abs(ref) + rtol * bound + floor_of(ours)
+    bad = diff > allowed
+    assert not bad.any(), (f"{what}: {int(bad.sum())}/{bad.size} elements off, worst excess "
+                           f"{float((diff - allowed).max()):.3g}")
 
 
-def head_grads_at(g, H, W, b, idx):
-    """fp64 torch-head gradient with the argmax fixed to `idx`."""
-    H64, W64 = np64(H), np64(W)
-    z = np.einsum("bvd,vd->bv", H64[np.arange(H64.shape[0])[:, None], idx], W64)
-    if b is not None:
-        z = z + np64(b)[None, :]
-    gp = np.where(z > 0, np64(g) / (1.0 + np.maximum(z, 0)), 0.0)
+def _grads(gp, H64, W64, idx, has_bias):
     B, S, D = H64.shape
     V = W64.shape[0]
     dW = np.zeros((V, D))
@@ -52,7 +59,20 @@ def head_grads_at(g, H, W, b, idx):
         P = np.zeros((S, V))
         P[idx[bb], np.arange(V)] = gp[bb]
         dH[bb] = P @ W64
-    return dH, dW, (gp.sum(0) if b is not None else None)
+    return dH, dW, (gp.sum(0) if has_bias else None)
+
+
+def head_grads_at(g, H, W, b, idx):
+    """fp64 torch-head gradient with the argmax fixed to `idx`, each paired with
+    the sum of the absolute values of its terms: ((dH, |dH|), (dW, |dW|), (db, |db|))."""
+    H64, W64 = np64(H), np64(W)
+    z = np.einsum("bvd,vd->bv", H64[np.arange(H64.shape[0])[:, None], idx], W64)
+    if b is not None:
+        z = z + np64(b)[None, :]
+    gp = np.where(z > 0, np64(g) / (1.0 + np.maximum(z, 0)), 0.0)
+    val = _grads(gp, H64, W64, idx, b is not None)
+    mag = _grads(np.abs(gp), np.abs(H64), np.abs(W64), idx, b is not None)
+    return tuple((v, m) for v, m in zip(val, mag))
 
 
 def run_fwd_bwd(H, W, b, mask, g):
@@ -120,10 +140,11 @@ def test_bwd_golden_fixtures(name):
     g = torch.tensor(c["g"]).float()
     reps, idx, dH, dW, db = run_fwd_bwd(H, W, b, mask, g)
     _, ref_idx, _ = orc.forward(c["H"], c["W"], c["bias"], c["mask"])
+    refs = head_grads_at(g, H, W, b, idx.numpy().astype(np.int64))
     if np.array_equal(idx.numpy(), ref_idx):
-        refs = (c["dH"], c["dW"], c["db"])
-    else:  # a near-tie resolved the other way: compare at our indices
-        refs = head_grads_at(g, H, W, b, idx.numpy().astype(np.int64))
+        # Same argmax as the reference run: compare with its own gradients,
+        # keeping the term-magnitude bound computed at our indices.
+        refs = tuple((r, m[1]) for r, m in zip((c["dH"], c["dW"], c["db"]), refs))
     close_to_head(dH, refs[0], 1e-5, "dH")
     close_to_head(dW, refs[1], 1e-5, "dW")
     if c["has_bias"]:
