@@ -189,6 +189,48 @@ def run_reference_arm(args, rank: int) -> int:
     return 0
 
 
+def e2e_bytes(H, mask, gs, B, Vs, dtype):
+    """Host<->device bytes per e2e step: the step's inputs in, reps out."""
+    h2d = (H.numel() * H.element_size() + mask.numel() * mask.element_size()
+           + gs.numel() * gs.element_size())
+    d2h = B * Vs * torch.empty((), dtype=dtype).element_size()
+    return h2d, d2h
+
+
+def run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier, max_over_ranks):
+    """ms per step of the public path: SpartonHead forward + autograd backward,
+    the step's inputs copied from pinned host memory and reps read back."""
+    from sparton_b200.head import SpartonHead
+
+    B, D, V = c["B"], c["D"], c["V"]
+    head = SpartonHead(V, D, use_bias=c["bias"], process_group=group).to(dev, c["dtype"])
+    head.load({"weight": W, "bias": b} if b is not None else {"weight": W})
+    H_pin, m_pin, g_pin = H.pin_memory(), mask.pin_memory(), gs.pin_memory()
+    reps_host = torch.empty(B, Vs, dtype=c["dtype"]).pin_memory()
+
+    def e2e_step():
+        hid = H_pin.to(dev, non_blocking=True).requires_grad_(True)
+        msk = m_pin.to(dev, non_blocking=True)
+        gg = g_pin.to(dev, non_blocking=True)
+        out = head(hid, msk)
+        out.backward(gg)
+        reps_host.copy_(out.detach(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        e2e_step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        e2e_step()
+        evs[i][1].record(stream)
+    barrier()
+    return max_over_ranks(sum(a.elapsed_time(e) for a, e in evs) / args.steps)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -196,10 +238,15 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU-baseline sample")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--legs", default="device,e2e,cpu",
+                    help="comma list of legs: device (value), e2e, cpu (baseline); "
+                         "profiling runs use --legs device")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    legs = set(args.legs.split(","))
+    if "device" not in legs:
+        ap.error("--legs must include device")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -214,14 +261,13 @@ def main(argv=None) -> int:
     import torch.distributed as dist
 
     from sparton_b200 import _lib
-    from sparton_b200.head import SpartonHead, VocabShard
+    from sparton_b200.head import VocabShard
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
 
     c = CFG
@@ -280,7 +326,7 @@ def main(argv=None) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
         return float(t.item())
 
-    # ---------------------------------------------------------------- device-resident
+    # ------------------------------------------------------------ device-resident
     for _ in range(args.warmup):
         flush.zero_()
         step()
@@ -298,42 +344,19 @@ def main(argv=None) -> int:
             step(*kern_ev[i])
             step_ev[i][1].record(stream)
         barrier()
-    step_ms = sum(a.elapsed_time(bb) for a, bb in step_ev) / args.steps
-    kern_ms = sum(a.elapsed_time(bb) for a, bb in kern_ev) / args.steps
-    step_ms = max_over_ranks(step_ms)
+    step_ms = max_over_ranks(sum(a.elapsed_time(e) for a, e in step_ev) / args.steps)
+    kern_ms = sum(a.elapsed_time(e) for a, e in kern_ev) / args.steps
     kern_ms_max = max_over_ranks(kern_ms)
     launches_per_step = 2 + (4 if bd is not None else 3)
 
-    # ---------------------------------------------------------------- end to end
-    head = SpartonHead(V, D, use_bias=c["bias"], process_group=group).to(dev, c["dtype"])
-    head.load({"weight": W, "bias": b} if b is not None else {"weight": W})
-    H_pin, m_pin, g_pin = H.pin_memory(), mask.pin_memory(), gs.pin_memory()
-    reps_host = torch.empty(B, Vs, dtype=c["dtype"]).pin_memory()
-    h2d = H_pin.numel() * H_pin.element_size() + m_pin.numel() * 8 + g_pin.numel() * g_pin.element_size()
-    d2h = reps_host.numel() * reps_host.element_size()
+    # ------------------------------------------------------------ end to end
+    e2e_ms = None
+    if "e2e" in legs:
+        e2e_ms = run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier,
+                         max_over_ranks)
+        h2d, d2h = e2e_bytes(H, mask, gs, B, Vs, c["dtype"])
 
-    def e2e_step():
-        hid = H_pin.to(dev, non_blocking=True).requires_grad_(True)
-        msk = m_pin.to(dev, non_blocking=True)
-        gg = g_pin.to(dev, non_blocking=True)
-        out = head(hid, msk)
-        out.backward(gg)
-        reps_host.copy_(out.detach(), non_blocking=True)
-
-    for _ in range(args.warmup):
-        flush.zero_()
-        e2e_step()
-    e2e_ev = [(ev(), ev()) for _ in range(args.steps)]
-    barrier()
-    for i in range(args.steps):
-        flush.zero_()
-        e2e_ev[i][0].record(stream)
-        e2e_step()
-        e2e_ev[i][1].record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(sum(a.elapsed_time(bb) for a, bb in e2e_ev) / args.steps)
-
-    # ---------------------------------------------------------------- report
+    # ------------------------------------------------------------ report
     peaks, peaks_src = load_peaks()
     fl = nominal_flops(c)
     value = fl / (step_ms * 1e-3) / 1e12
@@ -360,14 +383,15 @@ def main(argv=None) -> int:
                      "frac_of_sustained": round(achieved / float(peaks["bf16_tflops_sustained"]), 4),
                      "peak_source": f"{peaks_src} bf16_tflops (burst)",
                      "algorithmic_flops_per_launch": alg_fwd, "traffic": traffic},
-        "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "path": "SpartonHead forward + autograd backward, pinned host inputs"},
+        "e2e": None if e2e_ms is None else {
+            "value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "path": "SpartonHead forward + autograd backward, pinned host inputs"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and "cpu" in legs:
         try:
             res = cpu_baseline(c, args.cpu_rows, steps=3, warmup=1)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}

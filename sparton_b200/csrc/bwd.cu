@@ -11,11 +11,14 @@
 // one thread in a fixed order, so the result is deterministic:
 //   K2 bwd_sort_kernel   per batch row, a stable counting sort of the vocab ids
 //                        with score > 0 by their argmax position -> CSR
-//                        (offs[b][s] .. offs[b][s+1]) of (v, g') pairs.
-//   K3 dh_kernel         one warp per (b, s): dH[b,s,:] = sum over its bucket of
-//                        g' * W[v,:] (rows gathered, fp32 accumulation).
-//   K4 dw_kernel         one warp per v: dW[v,:] = sum_b g' * H[b, idx[b,v], :].
-//      db_kernel         one thread per v: db[v] = sum_b g'.
+//                        (offs[b][s] .. offs[b][s+1]) of (v, g') pairs; it also
+//                        writes the vocab-major list of (H row b*S+idx, g') that
+//                        dW reads.
+//   K3/K4 gather_reduce_kernel, one warp per output row:
+//                        dH[b,s,:] = sum over bucket (b,s) of g' * W[v,:]
+//                        dW[v,:]   = sum over b of g' * H[b*S + idx[b,v], :]
+//                        (+ db[v] = sum over b of g' in the same pass).
+//      db_kernel         db alone, when dW is not requested.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
@@ -130,8 +133,9 @@ __device__ __forceinline__ __half cvt_out<__half>(float x) {
 template <typename T>
 __global__ void __launch_bounds__(1024)
     bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
-                    const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
-                    int* __restrict__ perm, float* __restrict__ gperm) {
+                    const int32_t* __restrict__ idx, int B, int S, int V, int* __restrict__ offs,
+                    int* __restrict__ perm, float* __restrict__ gperm, int* __restrict__ wrow,
+                    float* __restrict__ wcoef) {
   extern __shared__ int cnt[];  // [nw][S]
   __shared__ int scan_tmp[33];
   const int b = blockIdx.x;
@@ -210,6 +214,13 @@ __global__ void __launch_bounds__(1024)
         gp = ld_f<T>(g + row + v) * expf(-sc);
       }
     }
+    if (v < v_end) {
+      // Vocab-major entry for dW: every (v, b) gets one, with g' = 0 when the
+      // head's output is 0 (the row index is then a harmless valid row).
+      const size_t t = static_cast<size_t>(v) * B + b;
+      wrow[t] = b * S + (key >= 0 ? key : 0);
+      wcoef[t] = gp;
+    }
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
     int slot = 0;
     if (key >= 0) slot = my[key] + __popc(peers & lt);
@@ -223,135 +234,142 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// ------------------------------------------------------------------ K3: dH
-// One warp per (b, s) row. A pass covers up to 1024 columns: lane l handles
-// columns d0 + c*256 + 8l .. +7 for c = 0..3. Bucket entries are processed
-// four at a time so four W rows are in flight per lane.
-template <typename T, typename O>
-__global__ void __launch_bounds__(256)
-    dh_kernel(const T* __restrict__ W, const int* __restrict__ offs, const int* __restrict__ perm,
-              const float* __restrict__ gperm, int B, int S, int D, int V, O* __restrict__ dH) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long rowid = static_cast<long long>(blockIdx.x) * 8 + warp;
-  if (rowid >= static_cast<long long>(B) * S) return;
-  const int b = static_cast<int>(rowid / S);
-  const int s = static_cast<int>(rowid % S);
-  const int* orow = offs + static_cast<size_t>(b) * (S + 1);
-  const int o0 = __ldg(orow + s), o1 = __ldg(orow + s + 1);
-  const int* pv = perm + static_cast<size_t>(b) * V;
-  const float* pg = gperm + static_cast<size_t>(b) * V;
-  O* out = dH + static_cast<size_t>(rowid) * D;
-  for (int d0 = 0; d0 < D; d0 += 1024) {
-    float acc[4][8];
+// --------------------------------------------------------- K3/K4: gather-reduce
+// out[r, :] = sum over the entry list of row r of coef[e] * src[row[e], :].
+//   kMode 0 (dH): r = b*S + s, list = bucket (b, s) of the CSR, src = W.
+//   kMode 1 (dW): r = v, list = the B entries of v, src = H; the coefficient
+//                 sum of the list is db[v].
+// One warp per output row. A pass covers NC*256 columns (lane l owns columns
+// d0 + c*256 + 8l .. +7). Entries are fetched 32 at a time with one coalesced
+// load and broadcast by shuffle; for each group of 4 entries every row load of
+// the pass is issued before the FMAs, so 4*NC 16-byte loads per lane are in
+// flight. Summation order is fixed: deterministic.
+template <typename T>
+struct Row8;
+template <>
+struct Row8<__nv_bfloat16> {
+  uint4 r;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) {
+    r = __ldg(reinterpret_cast<const uint4*>(p));
+  }
+  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
-    int e = o0;
-    for (; e + 4 <= o1; e += 4) {
-      int vv[4];
-      float gg[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        vv[u] = __ldg(pv + e + u);
-        gg[u] = __ldg(pg + e + u);
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int d = d0 + c * 256 + lane * 8;
-        if (d < D) {
-          float x[4][8];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) load8<T>(W + static_cast<size_t>(vv[u]) * D + d, x[u]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[c][i] = fmaf(gg[u], x[u][i], acc[c][i]);
-        }
-      }
-    }
-    for (; e < o1; ++e) {
-      const int v = __ldg(pv + e);
-      const float gv = __ldg(pg + e);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int d = d0 + c * 256 + lane * 8;
-        if (d < D) {
-          float x[8];
-          load8<T>(W + static_cast<size_t>(v) * D + d, x);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[c][i] = fmaf(gv, x[i], acc[c][i]);
-        }
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int d = d0 + c * 256 + lane * 8;
-      if (d < D) store8<O>(out + d, acc[c]);
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
+      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
     }
   }
-}
-
-// ------------------------------------------------------------------ K4: dW
-// One warp per vocab id, batch rows in order, four at a time.
-template <typename T, typename O>
-__global__ void __launch_bounds__(256)
-    dw_kernel(const T* __restrict__ g, const T* __restrict__ reps, const int32_t* __restrict__ idx,
-              const T* __restrict__ H, int B, int S, int D, int V, O* __restrict__ dW) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int v = blockIdx.x * 8 + warp;
-  if (v >= V) return;
-  O* out = dW + static_cast<size_t>(v) * D;
-  for (int d0 = 0; d0 < D; d0 += 1024) {
-    float acc[4][8];
+};
+template <>
+struct Row8<__half> {
+  uint4 r;
+  __device__ __forceinline__ void load(const __half* p) {
+    r = __ldg(reinterpret_cast<const uint4*>(p));
+  }
+  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
+      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
+    }
+  }
+};
+template <>
+struct Row8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    acc[0] = fmaf(c, a.x, acc[0]); acc[1] = fmaf(c, a.y, acc[1]);
+    acc[2] = fmaf(c, a.z, acc[2]); acc[3] = fmaf(c, a.w, acc[3]);
+    acc[4] = fmaf(c, b.x, acc[4]); acc[5] = fmaf(c, b.y, acc[5]);
+    acc[6] = fmaf(c, b.z, acc[6]); acc[7] = fmaf(c, b.w, acc[7]);
+  }
+};
+
+constexpr int kGatherWarps = 8;
+constexpr int kGatherUnroll = 4;
+
+template <typename T, typename O, int NC, int kMode>
+__global__ void __launch_bounds__(kGatherWarps * 32)
+    gather_reduce_kernel(const T* __restrict__ src, int D, int n_rows, int S, int V, int B,
+                         const int* __restrict__ offs, const int* __restrict__ ent_row,
+                         const float* __restrict__ ent_coef, O* __restrict__ out,
+                         O* __restrict__ out_sum) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kGatherWarps + warp;
+  if (r >= n_rows) return;
+  int e0, e1;
+  if (kMode == 0) {
+    const int b = r / S, s = r - (r / S) * S;
+    const int* o = offs + static_cast<size_t>(b) * (S + 1);
+    e0 = b * V + __ldg(o + s);
+    e1 = b * V + __ldg(o + s + 1);
+  } else {
+    e0 = r * B;
+    e1 = e0 + B;
+  }
+  O* orow = out + static_cast<size_t>(r) * D;
+  float csum = 0.f;
+  for (int d0 = 0; d0 < D; d0 += NC * 256) {
+    float acc[NC][8];
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
-    for (int b0 = 0; b0 < B; b0 += 4) {
-      float gg[4];
-      const T* rows[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        gg[u] = 0.f;
-        rows[u] = H;
-        const int b = b0 + u;
-        if (b < B) {
-          const size_t o = static_cast<size_t>(b) * V + v;
-          const float gp = scaled_grad<T>(g, reps, o);
-          const int s = __ldg(idx + o);
-          if (gp != 0.f && s >= 0 && s < S) {
-            gg[u] = gp;
-            rows[u] = H + (static_cast<size_t>(b) * S + s) * D;
-          }
-        }
+    for (int eb = e0; eb < e1; eb += 32) {
+      const int n = min(32, e1 - eb);
+      int my_row = 0;
+      float my_coef = 0.f;
+      if (lane < n) {
+        my_row = __ldg(ent_row + eb + lane);
+        my_coef = __ldg(ent_coef + eb + lane);
       }
+      if (kMode == 1 && d0 == 0) csum += my_coef;
+      for (int j = 0; j < n; j += kGatherUnroll) {
+        int rr[kGatherUnroll];
+        float cc[kGatherUnroll];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int d = d0 + c * 256 + lane * 8;
-        if (d < D) {
-          float x[4][8];
+        for (int u = 0; u < kGatherUnroll; ++u) {
+          rr[u] = __shfl_sync(0xFFFFFFFFu, my_row, j + u);
+          cc[u] = __shfl_sync(0xFFFFFFFFu, my_coef, j + u);
+        }
+        Row8<T> x[kGatherUnroll][NC];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (gg[u] != 0.f) {
-              load8<T>(rows[u] + d, x[u]);
-            } else {
+        for (int u = 0; u < kGatherUnroll; ++u)
 #pragma unroll
-              for (int i = 0; i < 8; ++i) x[u][i] = 0.f;
-            }
+          for (int c = 0; c < NC; ++c) {
+            const int d = d0 + c * 256 + lane * 8;
+            if (cc[u] != 0.f && d < D)
+              x[u][c].load(src + static_cast<size_t>(rr[u]) * D + d);
+            else
+              x[u][c].zero();
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kGatherUnroll; ++u)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[c][i] = fmaf(gg[u], x[u][i], acc[c][i]);
-        }
+          for (int c = 0; c < NC; ++c) x[u][c].fma_into(cc[u], acc[c]);
       }
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < NC; ++c) {
       const int d = d0 + c * 256 + lane * 8;
-      if (d < D) store8<O>(out + d, acc[c]);
+      if (d < D) store8<O>(orow + d, acc[c]);
     }
+  }
+  if (kMode == 1 && out_sum != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xFFFFFFFFu, csum, o);
+    if (lane == 0) out_sum[r] = cvt_out<O>(csum);
   }
 }
 
@@ -365,10 +383,32 @@ __global__ void __launch_bounds__(256) db_kernel(const T* __restrict__ g, const 
   db[v] = cvt_out<O>(acc);
 }
 
-template <typename T, typename O>
-int launch_dh(const void* grad_reps, const void* reps, const int32_t* idx, const void* weight,
-              int B, int S, int D, int V, void* d_hidden, const BwdWorkspace& ws,
-              cudaStream_t stream) {
+template <typename T, typename O, int kMode>
+int launch_gather(const T* src, int D, int n_rows, int S, int V, int B, const int* offs,
+                  const int* ent_row, const float* ent_coef, O* out, O* out_sum,
+                  cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>((n_rows + kGatherWarps - 1) / kGatherWarps);
+  const int block = kGatherWarps * 32;
+  if (D <= 256)
+    gather_reduce_kernel<T, O, 1, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
+                                                                     ent_row, ent_coef, out, out_sum);
+  else if (D <= 512)
+    gather_reduce_kernel<T, O, 2, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
+                                                                     ent_row, ent_coef, out, out_sum);
+  else if (D <= 768)
+    gather_reduce_kernel<T, O, 3, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
+                                                                     ent_row, ent_coef, out, out_sum);
+  else
+    gather_reduce_kernel<T, O, 4, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
+                                                                     ent_row, ent_coef, out, out_sum);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gather_reduce_kernel launch");
+  return SPARTON_OK;
+}
+
+template <typename T>
+int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int B, int S, int V,
+                const BwdWorkspace& ws, cudaStream_t stream) {
   int nw = 49152 / S;
   if (nw > 32) nw = 32;
   if (nw < 1) return fail(SPARTON_ERR_UNSUPPORTED, "backward supports S <= 49152 (got %d)", S);
@@ -380,34 +420,37 @@ int launch_dh(const void* grad_reps, const void* reps, const int32_t* idx, const
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd_sort_kernel)");
   }
   bwd_sort_kernel<T><<<B, nw * 32, smem, stream>>>(static_cast<const T*>(grad_reps),
-                                                   static_cast<const T*>(reps), idx, S, V, ws.offs,
-                                                   ws.perm, ws.gperm);
+                                                   static_cast<const T*>(reps), idx, B, S, V,
+                                                   ws.offs, ws.perm, ws.gperm, ws.wrow, ws.wcoef);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
-  const long long rows = static_cast<long long>(B) * S;
-  dh_kernel<T, O><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
-      static_cast<const T*>(weight), ws.offs, ws.perm, ws.gperm, B, S, D, V,
-      static_cast<O*>(d_hidden));
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "dh_kernel launch");
   return SPARTON_OK;
 }
 
-template <typename T, typename O>
-int launch_params(const void* grad_reps, const void* reps, const int32_t* idx, const void* hidden,
-                  int B, int S, int D, int V, void* d_weight, void* d_bias, cudaStream_t stream) {
-  const T* g = static_cast<const T*>(grad_reps);
-  const T* r = static_cast<const T*>(reps);
-  cudaError_t e;
-  if (d_weight != nullptr) {
-    dw_kernel<T, O><<<(V + 7) / 8, 256, 0, stream>>>(g, r, idx, static_cast<const T*>(hidden), B,
-                                                     S, D, V, static_cast<O*>(d_weight));
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "dw_kernel launch");
+template <typename T, typename OH, typename OP>
+int launch_all(const void* grad_reps, const void* reps, const int32_t* idx, const void* hidden,
+               const void* weight, int B, int S, int D, int V, void* d_hidden, void* d_weight,
+               void* d_bias, const BwdWorkspace& ws, cudaStream_t stream) {
+  if (d_hidden != nullptr || d_weight != nullptr) {
+    const int st = launch_sort<T>(grad_reps, reps, idx, B, S, V, ws, stream);
+    if (st != SPARTON_OK) return st;
   }
-  if (d_bias != nullptr) {
-    db_kernel<T, O><<<(V + 255) / 256, 256, 0, stream>>>(g, r, B, V, static_cast<O*>(d_bias));
-    e = cudaGetLastError();
+  if (d_hidden != nullptr) {
+    const int st = launch_gather<T, OH, 0>(static_cast<const T*>(weight), D, B * S, S, V, B,
+                                           ws.offs, ws.perm, ws.gperm, static_cast<OH*>(d_hidden),
+                                           nullptr, stream);
+    if (st != SPARTON_OK) return st;
+  }
+  if (d_weight != nullptr) {
+    const int st = launch_gather<T, OP, 1>(static_cast<const T*>(hidden), D, V, S, V, B, nullptr,
+                                           ws.wrow, ws.wcoef, static_cast<OP*>(d_weight),
+                                           static_cast<OP*>(d_bias), stream);
+    if (st != SPARTON_OK) return st;
+  } else if (d_bias != nullptr) {
+    db_kernel<T, OP><<<(V + 255) / 256, 256, 0, stream>>>(static_cast<const T*>(grad_reps),
+                                                          static_cast<const T*>(reps), B, V,
+                                                          static_cast<OP*>(d_bias));
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "db_kernel launch");
   }
   return SPARTON_OK;
@@ -418,19 +461,18 @@ int launch_in(const void* grad_reps, const void* reps, const int32_t* idx, const
               const void* weight, int B, int S, int D, int V, void* d_hidden, void* d_weight,
               void* d_bias, int dh_dtype, int dp_dtype, const BwdWorkspace& ws,
               cudaStream_t stream) {
-  if (d_hidden != nullptr) {
-    const int st =
-        dh_dtype == SPARTON_DTYPE_F32
-            ? launch_dh<T, float>(grad_reps, reps, idx, weight, B, S, D, V, d_hidden, ws, stream)
-            : launch_dh<T, T>(grad_reps, reps, idx, weight, B, S, D, V, d_hidden, ws, stream);
-    if (st != SPARTON_OK) return st;
-  }
-  if (d_weight == nullptr && d_bias == nullptr) return SPARTON_OK;
-  return dp_dtype == SPARTON_DTYPE_F32
-             ? launch_params<T, float>(grad_reps, reps, idx, hidden, B, S, D, V, d_weight, d_bias,
-                                       stream)
-             : launch_params<T, T>(grad_reps, reps, idx, hidden, B, S, D, V, d_weight, d_bias,
-                                   stream);
+  const bool hf = dh_dtype == SPARTON_DTYPE_F32, pf = dp_dtype == SPARTON_DTYPE_F32;
+  if (hf && pf)
+    return launch_all<T, float, float>(grad_reps, reps, idx, hidden, weight, B, S, D, V, d_hidden,
+                                       d_weight, d_bias, ws, stream);
+  if (hf)
+    return launch_all<T, float, T>(grad_reps, reps, idx, hidden, weight, B, S, D, V, d_hidden,
+                                   d_weight, d_bias, ws, stream);
+  if (pf)
+    return launch_all<T, T, float>(grad_reps, reps, idx, hidden, weight, B, S, D, V, d_hidden,
+                                   d_weight, d_bias, ws, stream);
+  return launch_all<T, T, T>(grad_reps, reps, idx, hidden, weight, B, S, D, V, d_hidden, d_weight,
+                             d_bias, ws, stream);
 }
 
 }  // namespace

@@ -60,16 +60,20 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
 // offs         B x (S+1) int32   bucket start of every position (CSR by position)
 // perm         B x V int32       vocab ids grouped by argmax position
 // gperm        B x V float       g' of those entries, same order
+// wrow         V x B int32       per vocab id: hidden row b*S + idx[b,v] of every b
+// wcoef        V x B float       per vocab id: g' of every b (0 when reps is 0)
 struct BwdWorkspace {
   unsigned int* status;
   int* offs;
   int* perm;
   float* gperm;
+  int* wrow;
+  float* wcoef;
 };
 
 inline size_t bwd_workspace_bytes(int64_t B, int64_t S, int64_t V) {
   return 256 + align256(static_cast<size_t>(B * (S + 1)) * 4) +
-         align256(static_cast<size_t>(B * V) * 4) + align256(static_cast<size_t>(B * V) * 4);
+         4 * align256(static_cast<size_t>(B * V) * 4);
 }
 
 inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t V) {
@@ -82,6 +86,10 @@ inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t 
   w.perm = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B * V) * 4);
   w.gperm = reinterpret_cast<float*>(base + off);
+  off += align256(static_cast<size_t>(B * V) * 4);
+  w.wrow = reinterpret_cast<int*>(base + off);
+  off += align256(static_cast<size_t>(B * V) * 4);
+  w.wcoef = reinterpret_cast<float*>(base + off);
   return w;
 }
 
