@@ -126,6 +126,32 @@ int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bia
                          void* reps, int32_t* idx,
                          void* workspace, size_t workspace_size, void* stream);
 
+/* Size of the scratch array compiled into the library for
+ * sparton_fwd_noalloc (1 MiB). It covers sparton_fwd_workspace_size(B,S,..)
+ * <= 1 MiB, i.e. roughly B * (S/8 + 4) <= 1,040,000 (B=4096 rows at S=2048). */
+#define SPARTON_FWD_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* sparton_fwd without a caller-provided workspace. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they run the head (a cgo / JNI host with no CUDA allocator of its own, a
+ * process whose framework already reserved the device memory for its pool, a
+ * loop that must not call cudaMalloc because it can synchronise the device).
+ * The scratch lives in a fixed __device__ array inside the library, one copy
+ * per GPU that loads it, held until the process exits; nothing is allocated.
+ * Arguments and results are those of sparton_fwd. Limits and caveats:
+ *  - sizes whose scratch exceeds SPARTON_FWD_NOALLOC_SCRATCH_BYTES are rejected
+ *    with SPARTON_ERR_UNSUPPORTED (use sparton_fwd then);
+ *  - every call on a device shares the one array: calls that overlap on the
+ *    GPU (e.g. on two streams without ordering between them) race and corrupt
+ *    each other; serialise them;
+ *  - the first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture begins. */
+int sparton_fwd_noalloc(const void* hidden, const void* weight, const void* bias,
+                        const void* mask, int mask_dtype, int dtype,
+                        int64_t B, int64_t S, int64_t D, int64_t V,
+                        void* reps, int32_t* idx, void* stream);
+
 /* --------------------------------------------------------------- backward */
 
 /* Bytes of workspace sparton_bwd needs. */

@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "sparton_fwd",
     "sparton_mask_prepare",
     "sparton_fwd_prepared",
+    "sparton_fwd_noalloc",
     "sparton_bwd_workspace_size",
     "sparton_bwd",
     "sparton_read_device_status",
@@ -65,6 +66,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_fwd_prepared.argtypes = [_vp, _vp, _vp, _i, _i64, _i64, _i64, _i64,
                                          _vp, _vp, _vp, _sz, _vp]
     lib.sparton_fwd_prepared.restype = _i
+    lib.sparton_fwd_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i64, _i64, _i64, _i64,
+                                        _vp, _vp, _vp]
+    lib.sparton_fwd_noalloc.restype = _i
     lib.sparton_bwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64,
                                 _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]
     lib.sparton_bwd.restype = _i
