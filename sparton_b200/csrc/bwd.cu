@@ -7,23 +7,25 @@
 // dW[v,:] += sum_b g' * H[b, idx[b,v], :] (:554-557) and, the dominant cost,
 // dH[b, idx[b,v], :] += g' * W[v,:] element by element (:559-561).
 //
-// Here the same sums are computed gather-side, each output element by exactly
-// one thread in a fixed order, so the result is deterministic:
-//   K2 bwd_sort_kernel   per batch row, a stable counting sort of the vocab ids
-//                        with score > 0 by their argmax position -> CSR
-//                        (offs[b][s] .. offs[b][s+1]) of (v, g') pairs; it also
-//                        writes the vocab-major list of (H row b*S+idx, g') that
-//                        dW reads.
-//   K3/K4 gather_reduce_kernel, one warp per output row:
-//                        dH[b,s,:] = sum over bucket (b,s) of g' * W[v,:]
-//                        dW[v,:]   = sum over b of g' * H[b*S + idx[b,v], :]
-//                        (+ db[v] = sum over b of g' in the same pass).
+// Here every output element is produced by exactly one warp in a fixed order
+// (deterministic, no atomics):
+//   K2 bwd_sort_kernel   per batch row: stable counting sort of the vocab ids with
+//                        score > 0 by argmax position -> CSR (offs[b][s]) of
+//                        (v, g') pairs, v ascending inside each bucket.
+//      dw_list_kernel    tiled transpose of (argmax row, g') to vocab-major
+//                        order: the B entries of each vocab id, contiguous.
+//   K3 gather_kernel<0>  one warp per (b, s) row: dH[b,s,:] = sum over its
+//                        bucket of g' * W[v,:] (W rows gathered, fp32 sums).
+//   K4 gather_kernel<1>  one warp per vocab id: dW[v,:] = sum over b of
+//                        g' * H[b*S + idx[b,v], :] (neighbouring vocab ids share
+//                        H[b] rows in L1); db[v] is the sum of the same g'.
 //      db_kernel         db alone, when dW is not requested.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace sparton {
 namespace {
@@ -50,37 +52,19 @@ __device__ __forceinline__ float scaled_grad(const T* g, const T* reps, size_t o
   return sc > 0.f ? ld_f<T>(g + o) * expf(-sc) : 0.f;
 }
 
-// Eight consecutive elements of a row -> fp32 (16-bit types: one 16-byte load).
-template <typename T>
-__device__ __forceinline__ void load8(const T* p, float (&x)[8]);
+template <typename O>
+__device__ __forceinline__ O cvt_out(float x);
 template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&x)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    x[2 * i] = f.x;
-    x[2 * i + 1] = f.y;
-  }
+__device__ __forceinline__ float cvt_out<float>(float x) {
+  return x;
 }
 template <>
-__device__ __forceinline__ void load8<__half>(const __half* p, float (&x)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    x[2 * i] = f.x;
-    x[2 * i + 1] = f.y;
-  }
+__device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
 }
 template <>
-__device__ __forceinline__ void load8<float>(const float* p, float (&x)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+__device__ __forceinline__ __half cvt_out<__half>(float x) {
+  return __float2half_rn(x);
 }
 
 template <typename O>
@@ -107,20 +91,70 @@ __device__ __forceinline__ void store8<__half>(__half* p, const float (&x)[8]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-template <typename O>
-__device__ __forceinline__ O cvt_out(float x);
+// Eight consecutive elements of a row (16-bit types: one 16-byte load; fp32:
+// two) and their FMA into eight fp32 accumulators.
+template <typename T>
+struct Row8;
 template <>
-__device__ __forceinline__ float cvt_out<float>(float x) {
-  return x;
-}
+struct Row8<__nv_bfloat16> {
+  uint4 r;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) {
+    r = __ldg(reinterpret_cast<const uint4*>(p));
+  }
+  __device__ __forceinline__ void load_smem(const __nv_bfloat16* p) {
+    r = *reinterpret_cast<const uint4*>(p);
+  }
+  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
+      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
+    }
+  }
+};
 template <>
-__device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) {
-  return __float2bfloat16_rn(x);
-}
+struct Row8<__half> {
+  uint4 r;
+  __device__ __forceinline__ void load(const __half* p) {
+    r = __ldg(reinterpret_cast<const uint4*>(p));
+  }
+  __device__ __forceinline__ void load_smem(const __half* p) {
+    r = *reinterpret_cast<const uint4*>(p);
+  }
+  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
+      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
+    }
+  }
+};
 template <>
-__device__ __forceinline__ __half cvt_out<__half>(float x) {
-  return __float2half_rn(x);
-}
+struct Row8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void load_smem(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
+    acc[0] = fmaf(c, a.x, acc[0]); acc[1] = fmaf(c, a.y, acc[1]);
+    acc[2] = fmaf(c, a.z, acc[2]); acc[3] = fmaf(c, a.w, acc[3]);
+    acc[4] = fmaf(c, b.x, acc[4]); acc[5] = fmaf(c, b.y, acc[5]);
+    acc[6] = fmaf(c, b.z, acc[6]); acc[7] = fmaf(c, b.w, acc[7]);
+  }
+};
+
 
 // ------------------------------------------------------------------ K2: sort
 // One block per batch row, `nw` warps. Warp w owns the contiguous vocab range
@@ -133,14 +167,14 @@ __device__ __forceinline__ __half cvt_out<__half>(float x) {
 template <typename T>
 __global__ void __launch_bounds__(1024)
     bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
-                    const int32_t* __restrict__ idx, int B, int S, int V, int* __restrict__ offs,
-                    int* __restrict__ perm, float* __restrict__ gperm, int* __restrict__ wrow,
-                    float* __restrict__ wcoef) {
+                    const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
+                    int* __restrict__ perm, float* __restrict__ gperm, unsigned int* status) {
   extern __shared__ int cnt[];  // [nw][S]
   __shared__ int scan_tmp[33];
   const int b = blockIdx.x;
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (b == 0 && threadIdx.x == 0) *status = 0u;
   for (int i = threadIdx.x; i < nw * S; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
 
@@ -165,7 +199,7 @@ __global__ void __launch_bounds__(1024)
 
   // Exclusive scan over positions of the per-position totals.
   const int per = (S + blockDim.x - 1) / blockDim.x;
-  const int k_begin = min(S, threadIdx.x * per), k_end = min(S, k_begin + per);
+  const int k_begin = min(S, static_cast<int>(threadIdx.x) * per), k_end = min(S, k_begin + per);
   int local = 0;
   for (int k = k_begin; k < k_end; ++k)
     for (int w = 0; w < nw; ++w) local += cnt[w * S + k];
@@ -214,13 +248,6 @@ __global__ void __launch_bounds__(1024)
         gp = ld_f<T>(g + row + v) * expf(-sc);
       }
     }
-    if (v < v_end) {
-      // Vocab-major entry for dW: every (v, b) gets one, with g' = 0 when the
-      // head's output is 0 (the row index is then a harmless valid row).
-      const size_t t = static_cast<size_t>(v) * B + b;
-      wrow[t] = b * S + (key >= 0 ? key : 0);
-      wcoef[t] = gp;
-    }
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
     int slot = 0;
     if (key >= 0) slot = my[key] + __popc(peers & lt);
@@ -234,79 +261,66 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// --------------------------------------------------------- K3/K4: gather-reduce
-// out[r, :] = sum over the entry list of row r of coef[e] * src[row[e], :].
-//   kMode 0 (dH): r = b*S + s, list = bucket (b, s) of the CSR, src = W.
-//   kMode 1 (dW): r = v, list = the B entries of v, src = H; the coefficient
-//                 sum of the list is db[v].
-// One warp per output row. A pass covers NC*256 columns (lane l owns columns
-// d0 + c*256 + 8l .. +7). Entries are fetched 32 at a time with one coalesced
-// load and broadcast by shuffle; for each group of 4 entries every row load of
-// the pass is issued before the FMAs, so 4*NC 16-byte loads per lane are in
-// flight. Summation order is fixed: deterministic.
+// Vocab-major list for dW: wrow[v*B + b] = b*S + idx[b,v] and wcoef[v*B + b] =
+// g'[b,v] (0, with a harmless valid row, when the head's output is 0). Tiles of
+// 32 batch rows x 32 vocab ids through shared memory: both sides coalesced.
 template <typename T>
-struct Row8;
-template <>
-struct Row8<__nv_bfloat16> {
-  uint4 r;
-  __device__ __forceinline__ void load(const __nv_bfloat16* p) {
-    r = __ldg(reinterpret_cast<const uint4*>(p));
+__global__ void __launch_bounds__(256)
+    dw_list_kernel(const T* __restrict__ g, const T* __restrict__ reps,
+                   const int32_t* __restrict__ idx, int B, int S, int V, int* __restrict__ wrow,
+                   float* __restrict__ wcoef, unsigned int* status) {
+  __shared__ float cs[32][33];
+  __shared__ int rs[32][33];
+  const int v0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  if (status != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *status = 0u;
+  for (int i = ty; i < 32; i += 8) {
+    const int b = b0 + i, v = v0 + tx;
+    float c = 0.f;
+    int r = b * S;
+    if (b < B && v < V) {
+      const size_t o = static_cast<size_t>(b) * V + v;
+      const int s = __ldg(idx + o);
+      c = scaled_grad<T>(g, reps, o);
+      if (s >= 0 && s < S) r += s; else c = 0.f;
+    }
+    cs[i][tx] = c;
+    rs[i][tx] = r;
   }
-  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
-  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
-      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int v = v0 + i, b = b0 + tx;
+    if (v < V && b < B) {
+      const size_t o = static_cast<size_t>(v) * B + b;
+      wrow[o] = rs[tx][i];
+      wcoef[o] = cs[tx][i];
     }
   }
-};
-template <>
-struct Row8<__half> {
-  uint4 r;
-  __device__ __forceinline__ void load(const __half* p) {
-    r = __ldg(reinterpret_cast<const uint4*>(p));
-  }
-  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
-  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
-    const __half2* h = reinterpret_cast<const __half2*>(&r);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(h[i]);
-      acc[2 * i] = fmaf(c, f.x, acc[2 * i]);
-      acc[2 * i + 1] = fmaf(c, f.y, acc[2 * i + 1]);
-    }
-  }
-};
-template <>
-struct Row8<float> {
-  float4 a, b;
-  __device__ __forceinline__ void load(const float* p) {
-    a = __ldg(reinterpret_cast<const float4*>(p));
-    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  }
-  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
-  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
-    acc[0] = fmaf(c, a.x, acc[0]); acc[1] = fmaf(c, a.y, acc[1]);
-    acc[2] = fmaf(c, a.z, acc[2]); acc[3] = fmaf(c, a.w, acc[3]);
-    acc[4] = fmaf(c, b.x, acc[4]); acc[5] = fmaf(c, b.y, acc[5]);
-    acc[6] = fmaf(c, b.z, acc[6]); acc[7] = fmaf(c, b.w, acc[7]);
-  }
-};
+}
 
-constexpr int kGatherWarps = 8;
-constexpr int kGatherUnroll = 4;
+// ----------------------------------------------------------- K3/K4: dH, dW
+// out[r,:] = sum over the entry list of row r of coef * src[row, :], one warp
+// per output row, 8 warps per CTA:
+//   kMode 0 (dH): r = b*S + s, entries = bucket (b, s) of the CSR
+//                 (src row = v, coef = g'), src = W;
+//   kMode 1 (dW): r = v, entries = its B vocab-major entries (src row =
+//                 b*S + idx[b,v], coef = g'), src = H; out_sum[r] = db[v].
+// A pass covers NC*256 columns (lane l owns columns d0 + c*256 + 8l .. +7).
+// Entries are fetched 32 at a time with one coalesced load and broadcast by
+// shuffle; for each group of 4 entries all row loads of the pass are issued
+// before the FMAs (4*NC 16-byte loads per lane in flight). For dW, neighbouring
+// vocab ids walk the batch rows in step, so the rows of H[b] they share are
+// served from L1.
+constexpr int kGWarps = 8;
+constexpr int kGUnroll = 4;
 
 template <typename T, typename O, int NC, int kMode>
-__global__ void __launch_bounds__(kGatherWarps * 32)
-    gather_reduce_kernel(const T* __restrict__ src, int D, int n_rows, int S, int V, int B,
-                         const int* __restrict__ offs, const int* __restrict__ ent_row,
-                         const float* __restrict__ ent_coef, O* __restrict__ out,
-                         O* __restrict__ out_sum) {
+__global__ void __launch_bounds__(kGWarps * 32)
+    gather_kernel(const T* __restrict__ src, int B, int S, int D, int V, const int* __restrict__ offs,
+                  const int* __restrict__ ent_row, const float* __restrict__ ent_coef, int n_rows,
+                  O* __restrict__ out, O* __restrict__ out_sum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kGatherWarps + warp;
+  const int r = blockIdx.x * kGWarps + warp;
   if (r >= n_rows) return;
   int e0, e1;
   if (kMode == 0) {
@@ -335,17 +349,17 @@ __global__ void __launch_bounds__(kGatherWarps * 32)
         my_coef = __ldg(ent_coef + eb + lane);
       }
       if (kMode == 1 && d0 == 0) csum += my_coef;
-      for (int j = 0; j < n; j += kGatherUnroll) {
-        int rr[kGatherUnroll];
-        float cc[kGatherUnroll];
+      for (int j = 0; j < n; j += kGUnroll) {
+        int rr[kGUnroll];
+        float cc[kGUnroll];
 #pragma unroll
-        for (int u = 0; u < kGatherUnroll; ++u) {
+        for (int u = 0; u < kGUnroll; ++u) {
           rr[u] = __shfl_sync(0xFFFFFFFFu, my_row, j + u);
           cc[u] = __shfl_sync(0xFFFFFFFFu, my_coef, j + u);
         }
-        Row8<T> x[kGatherUnroll][NC];
+        Row8<T> x[kGUnroll][NC];
 #pragma unroll
-        for (int u = 0; u < kGatherUnroll; ++u)
+        for (int u = 0; u < kGUnroll; ++u)
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             const int d = d0 + c * 256 + lane * 8;
@@ -355,7 +369,7 @@ __global__ void __launch_bounds__(kGatherWarps * 32)
               x[u][c].zero();
           }
 #pragma unroll
-        for (int u = 0; u < kGatherUnroll; ++u)
+        for (int u = 0; u < kGUnroll; ++u)
 #pragma unroll
           for (int c = 0; c < NC; ++c) x[u][c].fma_into(cc[u], acc[c]);
       }
@@ -383,27 +397,12 @@ __global__ void __launch_bounds__(256) db_kernel(const T* __restrict__ g, const 
   db[v] = cvt_out<O>(acc);
 }
 
-template <typename T, typename O, int kMode>
-int launch_gather(const T* src, int D, int n_rows, int S, int V, int B, const int* offs,
-                  const int* ent_row, const float* ent_coef, O* out, O* out_sum,
-                  cudaStream_t stream) {
-  const unsigned grid = static_cast<unsigned>((n_rows + kGatherWarps - 1) / kGatherWarps);
-  const int block = kGatherWarps * 32;
-  if (D <= 256)
-    gather_reduce_kernel<T, O, 1, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
-                                                                     ent_row, ent_coef, out, out_sum);
-  else if (D <= 512)
-    gather_reduce_kernel<T, O, 2, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
-                                                                     ent_row, ent_coef, out, out_sum);
-  else if (D <= 768)
-    gather_reduce_kernel<T, O, 3, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
-                                                                     ent_row, ent_coef, out, out_sum);
-  else
-    gather_reduce_kernel<T, O, 4, kMode><<<grid, block, 0, stream>>>(src, D, n_rows, S, V, B, offs,
-                                                                     ent_row, ent_coef, out, out_sum);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gather_reduce_kernel launch");
-  return SPARTON_OK;
+// ----------------------------------------------------------------------- host
+template <typename K>
+int set_smem(K kernel, int bytes, const char* what) {
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, what);
 }
 
 template <typename T>
@@ -413,38 +412,75 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
   if (nw > 32) nw = 32;
   if (nw < 1) return fail(SPARTON_ERR_UNSUPPORTED, "backward supports S <= 49152 (got %d)", S);
   const size_t smem = static_cast<size_t>(nw) * S * sizeof(int);
-  cudaError_t e;
   if (smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(bwd_sort_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd_sort_kernel)");
+    const int st = set_smem(bwd_sort_kernel<T>, static_cast<int>(smem),
+                            "cudaFuncSetAttribute(bwd_sort_kernel)");
+    if (st != SPARTON_OK) return st;
   }
   bwd_sort_kernel<T><<<B, nw * 32, smem, stream>>>(static_cast<const T*>(grad_reps),
-                                                   static_cast<const T*>(reps), idx, B, S, V,
-                                                   ws.offs, ws.perm, ws.gperm, ws.wrow, ws.wcoef);
-  e = cudaGetLastError();
+                                                   static_cast<const T*>(reps), idx, S, V,
+                                                   ws.offs, ws.perm, ws.gperm, ws.status);
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
   return SPARTON_OK;
+}
+
+template <typename T, typename O, int kMode>
+int launch_gather(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
+                  const float* ent_coef, int n_rows, O* out, O* out_sum, cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>((n_rows + kGWarps - 1) / kGWarps);
+  const int block = kGWarps * 32;
+  if (D <= 256)
+    gather_kernel<T, O, 1, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
+                                                              ent_coef, n_rows, out, out_sum);
+  else if (D <= 512)
+    gather_kernel<T, O, 2, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
+                                                              ent_coef, n_rows, out, out_sum);
+  else if (D <= 768)
+    gather_kernel<T, O, 3, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
+                                                              ent_coef, n_rows, out, out_sum);
+  else
+    gather_kernel<T, O, 4, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
+                                                              ent_coef, n_rows, out, out_sum);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gather_kernel launch");
+  return SPARTON_OK;
+}
+
+template <typename T, typename O>
+int launch_dh(const void* weight, int B, int S, int D, int V, void* d_hidden,
+              const BwdWorkspace& ws, cudaStream_t stream) {
+  return launch_gather<T, O, 0>(static_cast<const T*>(weight), B, S, D, V, ws.offs, ws.perm,
+                                ws.gperm, B * S, static_cast<O*>(d_hidden), nullptr, stream);
+}
+
+template <typename T, typename O>
+int launch_dw(const void* grad_reps, const void* reps, const int32_t* idx, const void* hidden,
+              int B, int S, int D, int V, void* d_weight, void* d_bias, const BwdWorkspace& ws,
+              cudaStream_t stream) {
+  const dim3 lgrid(static_cast<unsigned>((V + 31) / 32), static_cast<unsigned>((B + 31) / 32));
+  dw_list_kernel<T><<<lgrid, 256, 0, stream>>>(static_cast<const T*>(grad_reps),
+                                               static_cast<const T*>(reps), idx, B, S, V, ws.wrow,
+                                               ws.wcoef, ws.status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dw_list_kernel launch");
+  return launch_gather<T, O, 1>(static_cast<const T*>(hidden), B, S, D, V, nullptr, ws.wrow,
+                                ws.wcoef, V, static_cast<O*>(d_weight), static_cast<O*>(d_bias),
+                                stream);
 }
 
 template <typename T, typename OH, typename OP>
 int launch_all(const void* grad_reps, const void* reps, const int32_t* idx, const void* hidden,
                const void* weight, int B, int S, int D, int V, void* d_hidden, void* d_weight,
                void* d_bias, const BwdWorkspace& ws, cudaStream_t stream) {
-  if (d_hidden != nullptr || d_weight != nullptr) {
-    const int st = launch_sort<T>(grad_reps, reps, idx, B, S, V, ws, stream);
-    if (st != SPARTON_OK) return st;
-  }
   if (d_hidden != nullptr) {
-    const int st = launch_gather<T, OH, 0>(static_cast<const T*>(weight), D, B * S, S, V, B,
-                                           ws.offs, ws.perm, ws.gperm, static_cast<OH*>(d_hidden),
-                                           nullptr, stream);
+    int st = launch_sort<T>(grad_reps, reps, idx, B, S, V, ws, stream);
+    if (st == SPARTON_OK) st = launch_dh<T, OH>(weight, B, S, D, V, d_hidden, ws, stream);
     if (st != SPARTON_OK) return st;
   }
   if (d_weight != nullptr) {
-    const int st = launch_gather<T, OP, 1>(static_cast<const T*>(hidden), D, V, S, V, B, nullptr,
-                                           ws.wrow, ws.wcoef, static_cast<OP*>(d_weight),
-                                           static_cast<OP*>(d_bias), stream);
+    const int st =
+        launch_dw<T, OP>(grad_reps, reps, idx, hidden, B, S, D, V, d_weight, d_bias, ws, stream);
     if (st != SPARTON_OK) return st;
   } else if (d_bias != nullptr) {
     db_kernel<T, OP><<<(V + 255) / 256, 256, 0, stream>>>(static_cast<const T*>(grad_reps),

@@ -2,6 +2,7 @@
 // library: workspace layouts, launchers and error reporting. Not installed.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -18,6 +19,12 @@ int fail(int status, const char* fmt, ...);
 int cuda_fail(cudaError_t err, const char* what);
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// 2-D TMA tensor map over a row-major [outer][inner] array with `row_bytes`
+// between rows; box = [box_outer][box_inner] elements.
+int make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                       uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                       CUtensorMapSwizzle swizzle);
 
 // Number of SMs on the current device (cached per device).
 int device_sm_count();
