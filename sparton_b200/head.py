@@ -12,7 +12,8 @@ Keyword-only additions (defaults keep the upstream behaviour):
   ``[r*V_s, min(V, (r+1)*V_s))`` of the decoder, ``V_s = ceil(V/n)`` rounded up to
   the kernel's 128-row vocab tile. The forward needs no communication and
   returns ``reps[:, shard]``; the backward all-reduces (sum) the partial
-  d_hidden of every rank, in fp32 by default.
+  d_hidden of every rank, in ``grad_reduce_dtype`` (default: fp32 for 16-bit
+  inputs, the input dtype otherwise).
 * ``gather_output``: with a process group, all-gather the shards so forward
   returns the full ``reps[B, V]``.
 """
@@ -106,7 +107,7 @@ class SpartonHead(nn.Module):
 
     def __init__(self, vocab_size, hidden_dim, use_bias=False, *,
                  process_group: Optional[dist.ProcessGroup] = None, gather_output: bool = False,
-                 grad_reduce_dtype: torch.dtype = torch.float32):
+                 grad_reduce_dtype: Optional[torch.dtype] = None):
         super().__init__()
         self.vocab_size = int(vocab_size)
         self.hidden_dim = int(hidden_dim)
@@ -174,8 +175,12 @@ class SpartonHead(nn.Module):
             scores, _idx = torch.ops.sparton.fused_sparton_fwd(hidden_states, weight, bias,
                                                                attention_mask)
             return scores
+        reduce_dtype = self.grad_reduce_dtype
+        if reduce_dtype is None:
+            reduce_dtype = (torch.float32 if hidden_states.dtype in (torch.float16, torch.bfloat16)
+                            else hidden_states.dtype)
         reps = _ShardedHead.apply(hidden_states, weight, bias, attention_mask,
-                                  self.process_group, self.grad_reduce_dtype)
+                                  self.process_group, reduce_dtype)
         if self.gather_output:
             reps = _GatherVocab.apply(reps, self.shard, self.process_group)
         return reps

@@ -1,0 +1,115 @@
+"""Vocabulary-sharded SpartonHead on 2 CPU ranks (gloo): shard bounds, the forward
+without communication, the optional all-gather of reps, and the all-reduce of
+the partial d_hidden in the backward. The native operators are replaced inside
+the test by CPU stand-ins computed with the oracle, so what is tested is the
+host logic of the sharded path (partitioning, autograd wiring, collectives)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import sparton_oracle as orc
+from sparton_b200 import head as head_mod
+from sparton_b200 import ops
+from sparton_b200.head import SpartonHead, VocabShard
+
+B, S, D, V = 3, 11, 16, 300
+
+
+def _inputs():
+    gen = torch.Generator().manual_seed(7)
+    H = torch.randn(B, S, D, generator=gen, dtype=torch.float64)
+    W = torch.randn(V, D, generator=gen, dtype=torch.float64) * 0.3
+    b = torch.randn(V, generator=gen, dtype=torch.float64) * 0.05
+    L = torch.tensor([11, 4, 0])
+    mask = (torch.arange(S)[None, :] < L[:, None]).to(torch.int64)
+    g = torch.randn(B, V, generator=gen, dtype=torch.float64)
+    return H, W, b, mask, g
+
+
+def _cpu_forward(hidden, embed, bias, mask):
+    reps, idx, _ = orc.forward(hidden.detach().numpy(), embed.detach().numpy(),
+                               None if bias is None else bias.detach().numpy(), mask.numpy())
+    return torch.tensor(reps, dtype=hidden.dtype), torch.tensor(idx, dtype=torch.int32)
+
+
+def _cpu_backward(grad_out, scores, idx, hidden, embed, has_bias, need_hidden=True,
+                  need_embed=True, hidden_grad_dtype=None):
+    dH, dW, db = orc.backward_from_scores(grad_out.numpy(), scores.numpy(), idx.numpy(),
+                                          hidden.detach().numpy(), embed.detach().numpy(), has_bias)
+    gdt = hidden_grad_dtype or hidden.dtype
+    return (torch.tensor(dH, dtype=gdt) if need_hidden else None,
+            torch.tensor(dW, dtype=embed.dtype) if need_embed else None,
+            torch.tensor(db, dtype=embed.dtype) if has_bias else None)
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ops.forward_impl = _cpu_forward
+        ops.backward_impl = _cpu_backward
+        H, W, b, mask, g = _inputs()
+        for gather in (False, True):
+            head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD,
+                               gather_output=gather).double()
+            head.load({"weight": W, "bias": b})
+            sh = head.shard
+            hid = H.clone().requires_grad_(True)
+            reps = head(hid, mask)
+            if gather:
+                assert reps.shape == (B, V)
+                reps.backward(g)
+            else:
+                assert reps.shape == (B, sh.size)
+                reps.backward(g[:, sh.start:sh.stop])
+            np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_reps.npy"), reps.detach().numpy())
+            np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_dH.npy"), hid.grad.numpy())
+            np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_dW.npy"), head.weight.grad.numpy())
+            np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_db.npy"), head.bias.grad.numpy())
+            np.save(os.path.join(out_dir, f"r{rank}_shard.npy"), np.array([sh.start, sh.stop]))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_vocab_shard_bounds():
+    for world in (1, 2, 3, 4, 8):
+        shards = [VocabShard(30522, world, r) for r in range(world)]
+        assert shards[0].start == 0 and shards[-1].stop == 30522
+        for a, c in zip(shards, shards[1:]):
+            assert a.stop == c.start
+        if world > 1:
+            assert all(s.padded % head_mod.VOCAB_TILE == 0 for s in shards)
+    tiny = [VocabShard(100, 4, r) for r in range(4)]  # more ranks than tiles: empty shards
+    assert [t.size for t in tiny] == [100, 0, 0, 0]
+
+
+def test_sharded_head_two_ranks(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    H, W, b, mask, g = _inputs()
+    reps, idx, _ = orc.forward(H.numpy(), W.numpy(), b.numpy(), mask.numpy())
+    dH, dW, db = orc.backward_from_scores(g.numpy(), reps, idx, H.numpy(), W.numpy(), True)
+    for gather in (0, 1):
+        for r in range(world):
+            lo, hi = np.load(tmp_path / f"r{r}_shard.npy")
+            got = np.load(tmp_path / f"r{r}_g{gather}_reps.npy")
+            np.testing.assert_allclose(got, reps if gather else reps[:, lo:hi], rtol=1e-12)
+            # every rank holds the full d_hidden after the all-reduce
+            np.testing.assert_allclose(np.load(tmp_path / f"r{r}_g{gather}_dH.npy"), dH,
+                                       rtol=1e-10, atol=1e-12)
+            np.testing.assert_allclose(np.load(tmp_path / f"r{r}_g{gather}_dW.npy"), dW[lo:hi],
+                                       rtol=1e-10, atol=1e-12)
+            np.testing.assert_allclose(np.load(tmp_path / f"r{r}_g{gather}_db.npy"), db[lo:hi],
+                                       rtol=1e-10, atol=1e-12)
