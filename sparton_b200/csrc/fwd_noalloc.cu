@@ -2,7 +2,7 @@
 // allocate device memory.
 //
 // sparton_fwd needs a small scratch buffer from its caller (per-row validity
-// bits, row extents, the status word and the scheduler's counters). Some
+// bits, row extents and the status word). Some
 // callers cannot provide one at the point where they run the head: a Go or Java
 // service that binds this C ABI through cgo / JNI and has no CUDA allocator of
 // its own; a serving process whose framework has already reserved (nearly) all
@@ -68,8 +68,8 @@ extern "C" int sparton_fwd_noalloc(const void* hidden, const void* weight, const
   void* ws = nullptr;
   const int st = scratch_address(&ws);
   if (st != SPARTON_OK) return st;
-  // The forward resets everything in the scratch that must start at zero (status
-  // word and scheduler counters) and overwrites the bits / extents it reads.
+  // The forward resets everything in the scratch that must start at zero (the
+  // status word) and overwrites the bits / extents it reads.
   return sparton_fwd(hidden, weight, bias, mask, mask_dtype, dtype, B, S, D, V, reps, idx, ws,
                      SPARTON_FWD_NOALLOC_SCRATCH_BYTES, stream);
 }

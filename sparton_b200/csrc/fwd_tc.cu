@@ -14,21 +14,28 @@
 // sequence: the max / argmax over S needs no cross-thread reduction.
 //
 // Work unit = (vocab tile of 128, batch row b). The unit covers positions
-// [0, E_b) in s-tiles of <= 256, where E_b is the last valid position + 1;
-// the MMA N of the last s-tile is rounded up to 16 only, so padded positions
-// beyond E_b cost nothing. Units are handed out by an atomic counter
-// (dynamic persistent scheduling), in panel order: panels of `panel_b` batch
-// rows whose hidden states fit in L2, vocab-tile-major inside a panel.
+// [0, E_b) in s-tiles of <= 256, where E_b is the last valid position + 1.
+// The MMA N of an s-tile is its width rounded up to 16, and the hidden rows
+// of one K step arrive in ONE TMA box of exactly that many rows (16 tensor
+// maps, boxes of 16, 32, ..., 256 rows), so padded positions cost nothing and
+// a stage is two TMA requests. Units go round-robin over the CTAs (CTA i
+// takes units i, i + grid, ...). Order: panels of `panel_b` batch rows whose
+// hidden states fit in L2; inside a panel, groups of `group_b` rows; inside a
+// group, vocab-tile-major. Every role of a CTA walks the same unit sequence,
+// so no unit ids pass between them.
 //
 // Warp roles (192 threads, one CTA per SM):
-//   warp 0    TMA producer: W tile [128 x 64] + hidden tile [<=256 x 64] per
+//   warp 0    TMA producer: W tile [128 x 64] + hidden tile [N x 64] per
 //             stage, 4 stages, 128-byte swizzle.
 //   warp 1    TMEM owner + MMA issuer: tcgen05.mma kind::f16, fp32 accumulator
 //             in TMEM, two 256-column accumulators (MMA of the next s-tile
 //             overlaps the epilogue of the previous one).
-//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time, masked running max and
+//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time (the next chunk's load
+//             in flight while one is scanned), masked running max and
 //             first-index argmax over positions (strict >, as upstream
 //             :150-156), then bias, relu, log1p and the stores of reps / idx.
+//             The s-tile's mask words and the unit's bias are fetched before
+//             the wait for the accumulator, off the critical path.
 //
 // Every wait is bounded (ptx.cuh); on timeout the CTA records a status code,
 // drains its in-flight TMA copies and MMAs, frees TMEM and exits.
@@ -49,40 +56,44 @@ constexpr int kBM = 128;        // vocab rows per tile = MMA M = TMEM lanes
 constexpr int kBN = 256;        // max positions per s-tile = MMA N
 constexpr int kBK = 64;         // K elements per stage: 128-byte rows
 constexpr int kStages = 4;      // TMA -> MMA pipeline depth
-constexpr int kBoxRows = 64;    // hidden rows per TMA box
-constexpr int kABytes = kBM * kBK * 2;
-constexpr int kBBytes = kBN * kBK * 2;
-constexpr int kBoxBytes = kBoxRows * kBK * 2;
+constexpr int kRowBytes = kBK * 2;
+constexpr int kABytes = kBM * kRowBytes;
+constexpr int kBBytes = kBN * kRowBytes;
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kSchedSlots = 4;  // unit ids in flight between roles
+constexpr int kNumHiddenMaps = kBN / 16;  // boxes of 16, 32, ..., 256 rows
 constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kNumAcc * kBN;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kTileWords = kBN / 32;  // mask words per s-tile
+// Batch rows per unit group inside an L2 panel (0: the whole panel).
+constexpr int kRowGroup = 0;
 
 // Barrier indices inside the barrier block.
 constexpr int kBarFull = 0;
 constexpr int kBarEmpty = kBarFull + kStages;
 constexpr int kBarTFull = kBarEmpty + kStages;
 constexpr int kBarTEmpty = kBarTFull + kNumAcc;
-constexpr int kBarSFull = kBarTEmpty + kNumAcc;
-constexpr int kBarSEmpty = kBarSFull + kSchedSlots;
-constexpr int kBarDrain = kBarSEmpty + kSchedSlots;
+constexpr int kBarDrain = kBarTEmpty + kNumAcc;
 constexpr int kNumBars = kBarDrain + 1;
 
-constexpr int kCtrlOffset = kStages * kStageBytes;         // barriers + slots
-constexpr int kSlotOffset = kCtrlOffset + kNumBars * 8;    // long long[kSchedSlots]
-constexpr int kTmemHolderOffset = kSlotOffset + kSchedSlots * 8;
+constexpr int kCtrlOffset = kStages * kStageBytes;  // barriers, TMEM address, abort flag
+constexpr int kTmemHolderOffset = kCtrlOffset + kNumBars * 8;
 constexpr int kAbortOffset = kTmemHolderOffset + 4;
 constexpr int kCtrlBytes = 512;
 static_assert(kAbortOffset + 4 <= kCtrlOffset + kCtrlBytes, "control block overflow");
 constexpr int kSmemBytes = kCtrlOffset + kCtrlBytes + 1024;  // + alignment slack
+
+struct alignas(64) HiddenMaps {
+  CUtensorMap m[kNumHiddenMaps];  // m[i]: boxes of 16 * (i + 1) rows x 64 columns
+};
 
 struct FwdTcParams {
   int B, S, D, V;
   int num_vtiles;
   int num_kblocks;
   int panel_b;
+  int group_b;
   long long num_units;
   const uint32_t* bits;
   int S32;
@@ -90,8 +101,6 @@ struct FwdTcParams {
   const void* bias;
   void* reps;
   int32_t* idx;
-  unsigned int* counter;  // next unit to hand out (minus gridDim.x)
-  unsigned int* done;     // CTAs finished; the last one resets both counters
   unsigned int* status;
 };
 
@@ -122,13 +131,18 @@ __device__ __forceinline__ void decode_unit(long long j, const FwdTcParams& p, i
   const long long r = j - panel * per_panel;
   const int b0 = static_cast<int>(panel * p.panel_b);
   const int pb = min(p.panel_b, p.B - b0);
-  vt = static_cast<int>(r / pb);
-  b = b0 + static_cast<int>(r % pb);
+  // Row groups of group_b rows (the last may be shorter); every group before
+  // the one holding r is full.
+  const long long per_group = static_cast<long long>(p.num_vtiles) * p.group_b;
+  const int g = static_cast<int>(r / per_group);
+  const int rr = static_cast<int>(r - g * per_group);
+  const int gb = min(p.group_b, pb - g * p.group_b);
+  vt = rr / gb;
+  b = b0 + g * p.group_b + rr % gb;
 }
 
 struct Ctrl {
   uint32_t bar0;  // shared address of barrier 0
-  long long* slots;
   volatile int* abort_flag;
   __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * i; }
 };
@@ -138,30 +152,15 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
   int stage = 0;
   uint32_t phase = 0;
   uint32_t issued_mask = 0, issued_parity = 0;
-  long long j = blockIdx.x;
-  int k = 0;
   bool ok = true;
-  while (true) {
-    const int slot = k % kSchedSlots;
-    const uint32_t sph = (k / kSchedSlots) & 1;
-    if (!mbar_wait_bounded(c.bar(kBarSEmpty + slot), sph ^ 1, c.abort_flag, p.status,
-                           SPARTON_DEV_TIMEOUT_PRODUCER)) {
-      ok = false;
-      break;
-    }
-    const long long unit = j < p.num_units ? j : -1;
-    c.slots[slot] = unit;
-    mbar_arrive(c.bar(kBarSFull + slot));
-    ++k;
-    if (unit < 0) break;
-    const long long next = static_cast<long long>(atomicAdd(p.counter, 1u)) + gridDim.x;
+  for (long long j = blockIdx.x; j < p.num_units && ok; j += gridDim.x) {
     int vt, b;
-    decode_unit(unit, p, vt, b);
-    const int E = p.extent[b];
+    decode_unit(j, p, vt, b);
+    const int E = __ldg(p.extent + b);
     for (int s0 = 0; s0 < E && ok; s0 += kBN) {
-      const int ncols = min(kBN, E - s0);
-      const int nbox = (ncols + kBoxRows - 1) / kBoxRows;
-      const uint32_t bytes = kABytes + nbox * kBoxBytes;
+      const int n16 = (min(kBN, E - s0) + 15) >> 4;  // hidden rows / 16
+      const uint32_t bytes = static_cast<uint32_t>(kABytes + n16 * 16 * kRowBytes);
+      const CUtensorMap* map = tmH + (n16 - 1);
       const int row0 = b * p.S + s0;
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
         if (!mbar_wait_bounded(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
@@ -173,8 +172,7 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
         mbar_arrive_expect_tx(full, bytes);
         const uint32_t a_dst = stage_base + stage * kStageBytes;
         tma_load_2d(a_dst, tmW, full, kb * kBK, vt * kBM);
-        for (int i = 0; i < nbox; ++i)
-          tma_load_2d(a_dst + kABytes + i * kBoxBytes, tmH, full, kb * kBK, row0 + i * kBoxRows);
+        tma_load_2d(a_dst + kABytes, map, full, kb * kBK, row0);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == kStages) {
@@ -183,15 +181,14 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
         }
       }
     }
-    if (!ok) break;
-    j = next;
   }
-  if (!ok) {
-    // Unwinding: let every issued copy land before the CTA's shared memory goes away.
-    for (int s = 0; s < kStages; ++s)
-      if (issued_mask & (1u << s))
-        if (!mbar_wait_drain(c.bar(kBarFull + s), (issued_parity >> s) & 1))
-          atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
+  for (int s = 0; s < kStages; ++s) {
+    if (!(issued_mask & (1u << s))) continue;
+    const uint32_t par = (issued_parity >> s) & 1;
+    // Normal end: the MMA's last commits to `empty` have landed before the CTA
+    // may exit. Unwinding: every issued copy has landed.
+    const uint32_t bar = c.bar((ok ? kBarEmpty : kBarFull) + s);
+    if (!mbar_wait_drain(bar, par)) atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
   }
 }
 
@@ -201,24 +198,12 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
   int stage = 0;
   uint32_t phase = 0;
   uint32_t tile = 0;
-  int k = 0;
   bool ok = true;
   bool issued = false;
-  while (ok) {
-    const int slot = k % kSchedSlots;
-    const uint32_t sph = (k / kSchedSlots) & 1;
-    if (!mbar_wait_bounded(c.bar(kBarSFull + slot), sph, c.abort_flag, p.status,
-                           SPARTON_DEV_TIMEOUT_MMA)) {
-      ok = false;
-      break;
-    }
-    const long long unit = c.slots[slot];
-    mbar_arrive(c.bar(kBarSEmpty + slot));
-    ++k;
-    if (unit < 0) break;
+  for (long long j = blockIdx.x; j < p.num_units && ok; j += gridDim.x) {
     int vt, b;
-    decode_unit(unit, p, vt, b);
-    const int E = p.extent[b];
+    decode_unit(j, p, vt, b);
+    const int E = __ldg(p.extent + b);
     for (int s0 = 0; s0 < E; s0 += kBN) {
       const int acc = tile & 1;
       const uint32_t aph = (tile >> 1) & 1;
@@ -228,8 +213,7 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
         break;
       }
       tc_fence_after_sync();
-      const uint32_t ncols = static_cast<uint32_t>(min(kBN, E - s0));
-      const uint32_t n_mma = (ncols + 15u) & ~15u;
+      const uint32_t n_mma = static_cast<uint32_t>((min(kBN, E - s0) + 15) & ~15);
       const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma);
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
@@ -265,6 +249,29 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
   }
 }
 
+// Folds 32 consecutive positions (one TMEM chunk, mask word `mw`, first
+// position `pos0`) into the running masked max / first argmax.
+__device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw, int pos0,
+                                           float& best, int& best_idx) {
+  if (mw == 0u) return;
+  float cm = -INFINITY;
+  if (mw == 0xFFFFFFFFu) {
+#pragma unroll
+    for (int q = 0; q < 32; ++q) cm = fmaxf(cm, __uint_as_float(r[q]));
+  } else {
+#pragma unroll
+    for (int q = 0; q < 32; ++q) cm = ((mw >> q) & 1u) ? fmaxf(cm, __uint_as_float(r[q])) : cm;
+  }
+  if (cm > best) {
+    int first = 31;
+#pragma unroll
+    for (int q = 31; q >= 0; --q)
+      if (((mw >> q) & 1u) && __uint_as_float(r[q]) == cm) first = q;
+    best = cm;
+    best_idx = pos0 + first;
+  }
+}
+
 template <typename T>
 __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
                              int lane) {
@@ -272,59 +279,47 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
   const int row = quad * 32 + lane;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
   uint32_t tile = 0;
-  int k = 0;
-  while (true) {
-    const int slot = k % kSchedSlots;
-    const uint32_t sph = (k / kSchedSlots) & 1;
-    if (!mbar_wait_bounded(c.bar(kBarSFull + slot), sph, c.abort_flag, p.status,
-                           SPARTON_DEV_TIMEOUT_EPILOGUE))
-      break;
-    const long long unit = c.slots[slot];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(c.bar(kBarSEmpty + slot));
-    ++k;
-    if (unit < 0) break;
+  for (long long j = blockIdx.x; j < p.num_units; j += gridDim.x) {
     int vt, b;
-    decode_unit(unit, p, vt, b);
-    const int E = p.extent[b];
+    decode_unit(j, p, vt, b);
+    const int E = __ldg(p.extent + b);
+    const int v = vt * kBM + row;
     const uint32_t* bits_row = p.bits + static_cast<size_t>(b) * p.S32;
+    const float bias = (p.bias != nullptr && v < p.V)
+                           ? to_float<T>(static_cast<const T*>(p.bias)[v])
+                           : 0.f;
     float best = -INFINITY;
     int best_idx = 0;
     bool ok = true;
     for (int s0 = 0; s0 < E; s0 += kBN) {
+      // Lane i holds mask word i of this s-tile (positions s0 + 32i ...).
+      const int w0 = s0 >> 5;
+      const uint32_t words =
+          (lane < kTileWords && w0 + lane < p.S32) ? __ldg(bits_row + w0 + lane) : 0u;
       const int acc = tile & 1;
       const uint32_t aph = (tile >> 1) & 1;
-      if (!mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
-                             SPARTON_DEV_TIMEOUT_EPILOGUE)) {
+      // The whole warp leaves together (the TMEM loads below are warp-wide),
+      // even if a wait gave up in only some of its lanes.
+      const bool got = mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
+                                         SPARTON_DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xFFFFFFFFu, got)) {
         ok = false;
         break;
       }
       tc_fence_after_sync();
-      const int ncols = min(kBN, E - s0);
+      const int nch = (min(kBN, E - s0) + 31) >> 5;
       const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * kBN);
-      for (int c0 = 0; c0 < ncols; c0 += 32) {
-        const uint32_t mw = __ldg(bits_row + ((s0 + c0) >> 5));
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c0), r);
-        tmem_ld_wait();
-        if (mw == 0u) continue;
-        float cm = -INFINITY;
-        if (mw == 0xFFFFFFFFu) {
-#pragma unroll
-          for (int q = 0; q < 32; ++q) cm = fmaxf(cm, __uint_as_float(r[q]));
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q)
-            cm = ((mw >> q) & 1u) ? fmaxf(cm, __uint_as_float(r[q])) : cm;
-        }
-        if (cm > best) {
-          int first = 31;
-#pragma unroll
-          for (int q = 31; q >= 0; --q)
-            if (((mw >> q) & 1u) && __uint_as_float(r[q]) == cm) first = q;
-          best = cm;
-          best_idx = s0 + c0 + first;
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(taddr, ra);
+      for (int ch = 0; ch < nch; ch += 2) {
+        tmem_ld_wait(ra);
+        if (ch + 1 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 1)), rb);
+        scan_chunk(ra, __shfl_sync(0xFFFFFFFFu, words, ch), s0 + 32 * ch, best, best_idx);
+        if (ch + 1 < nch) {
+          tmem_ld_wait(rb);
+          if (ch + 2 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 2)), ra);
+          scan_chunk(rb, __shfl_sync(0xFFFFFFFFu, words, ch + 1), s0 + 32 * (ch + 1), best,
+                     best_idx);
         }
       }
       tc_fence_before_sync();
@@ -333,11 +328,9 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
       ++tile;
     }
     if (!ok) break;
-    const int v = vt * kBM + row;
     if (v < p.V) {
       // max_s(x_s + bias) = max_s(x_s) + bias: the bias is added once, after the
       // max. Upstream's initial value 0 (:112) is the `logit > 0` test.
-      const float bias = p.bias != nullptr ? to_float<T>(static_cast<const T*>(p.bias)[v]) : 0.f;
       const float logit = best + bias;
       const bool pos = logit > 0.f;
       const size_t o = static_cast<size_t>(b) * p.V + v;
@@ -349,7 +342,7 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
 
 template <typename T, uint32_t kFmt>
 __global__ void __launch_bounds__(kThreads, 1)
-    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ HiddenMaps tmH,
                   const FwdTcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -357,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t stage_base = smem_addr(smem);
   Ctrl c;
   c.bar0 = stage_base + kCtrlOffset;
-  c.slots = reinterpret_cast<long long*>(smem + kSlotOffset);
   c.abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOffset);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kTmemHolderOffset);
 
@@ -373,10 +365,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(c.bar(kBarTFull + a), 1);
       mbar_init(c.bar(kBarTEmpty + a), kEpiWarps);
     }
-    for (int s = 0; s < kSchedSlots; ++s) {
-      mbar_init(c.bar(kBarSFull + s), 1);
-      mbar_init(c.bar(kBarSEmpty + s), 1 + kEpiWarps);
-    }
     mbar_init(c.bar(kBarDrain), 1);
     *c.abort_flag = 0;
     fence_barrier_init();
@@ -384,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
-    tma_prefetch_desc(&tmH);
+    for (int i = 0; i < kNumHiddenMaps; ++i) tma_prefetch_desc(&tmH.m[i]);
   }
   if (warp == 1) {
     tmem_alloc(smem_addr(tmem_holder), kTmemCols);
@@ -396,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
-    if (lane == 0) run_producer(p, &tmW, &tmH, stage_base, c);
+    if (lane == 0) run_producer(p, &tmW, tmH.m, stage_base, c);
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) run_mma<kFmt>(p, stage_base, tmem_base, c);
@@ -411,15 +399,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (threadIdx.x == 0) {
-    // Leave the scheduler counters at zero so the same prepared workspace can
-    // be launched again.
-    __threadfence();
-    if (atomicAdd(p.done, 1u) == gridDim.x - 1) {
-      atomicExch(p.counter, 0u);
-      atomicExch(p.done, 0u);
-    }
-  }
 }
 
 // ----------------------------------------------------------------------- host
@@ -433,13 +412,17 @@ template <typename T, uint32_t kFmt>
 int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight, const void* bias,
                  int B, int S, int D, int V, void* reps, int32_t* idx, const FwdWorkspace& ws,
                  cudaStream_t stream) {
-  CUtensorMap tmW, tmH;
+  CUtensorMap tmW;
+  HiddenMaps tmH;
   int st = make_map_2d(&tmW, dt, weight, static_cast<uint64_t>(D), static_cast<uint64_t>(V), kBK,
                        kBM);
   if (st != SPARTON_OK) return st;
-  st = make_map_2d(&tmH, dt, hidden, static_cast<uint64_t>(D),
-                   static_cast<uint64_t>(B) * static_cast<uint64_t>(S), kBK, kBoxRows);
-  if (st != SPARTON_OK) return st;
+  for (int i = 0; i < kNumHiddenMaps; ++i) {
+    st = make_map_2d(&tmH.m[i], dt, hidden, static_cast<uint64_t>(D),
+                     static_cast<uint64_t>(B) * static_cast<uint64_t>(S), kBK,
+                     static_cast<uint32_t>(16 * (i + 1)));
+    if (st != SPARTON_OK) return st;
+  }
 
   FwdTcParams p;
   p.B = B;
@@ -454,6 +437,7 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
   if (pb < 1) pb = 1;
   if (pb > B) pb = B;
   p.panel_b = static_cast<int>(pb);
+  p.group_b = (kRowGroup > 0 && kRowGroup < p.panel_b) ? kRowGroup : p.panel_b;
   p.num_units = static_cast<long long>(p.num_vtiles) * B;
   p.bits = ws.bits;
   p.S32 = ws.S32;
@@ -461,8 +445,6 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
   p.bias = bias;
   p.reps = reps;
   p.idx = idx;
-  p.counter = ws.counter;
-  p.done = ws.done;
   p.status = ws.status;
 
   static std::mutex mu;

@@ -33,13 +33,11 @@ int device_sm_count();
 bool device_is_sm100();
 
 // ------------------------------------------------------------ forward workspace
-// [0,256)      header: u32 status, u32 tile counter, u32 finished-CTA counter
+// [0,256)      header: u32 status, then reserved words (zeroed with it)
 // extents      B x int32      last valid position + 1 of each row (0 = empty)
 // bits         B x S32 x u32  validity bit of every position, S32 = ceil(S/32)
 struct FwdWorkspace {
   unsigned int* status;
-  unsigned int* counter;
-  unsigned int* done;
   int* extent;
   uint32_t* bits;
   int S32;
@@ -54,8 +52,6 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
   FwdWorkspace w;
   char* base = static_cast<char*>(ws);
   w.status = reinterpret_cast<unsigned int*>(base);
-  w.counter = reinterpret_cast<unsigned int*>(base) + 1;
-  w.done = reinterpret_cast<unsigned int*>(base) + 2;
   w.extent = reinterpret_cast<int*>(base + 256);
   w.bits = reinterpret_cast<uint32_t*>(base + 256 + align256(static_cast<size_t>(B) * 4));
   w.S32 = static_cast<int>((S + 31) / 32);

@@ -27,8 +27,8 @@ __device__ __forceinline__ bool is_valid<__nv_bfloat16>(__nv_bfloat16 m) {
   return __bfloat162float(m) != 0.f;
 }
 
-// One block per batch row. Also resets the workspace header (status word and
-// the persistent kernel's scheduler counters) so the main kernel starts clean.
+// One block per batch row. Also resets the workspace header (the status word
+// and the reserved words after it) so the main kernel starts clean.
 template <typename M>
 __global__ void __launch_bounds__(256) mask_prepare_kernel(const M* __restrict__ mask, int S, int S32,
                                                            uint32_t* __restrict__ bits,
