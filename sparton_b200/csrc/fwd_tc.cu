@@ -143,6 +143,40 @@ __device__ __forceinline__ void decode_unit(long long j, const FwdTcParams& p, i
   b = b0 + g * p.group_b + rr % gb;
 }
 
+// Walks the units of this CTA (blockIdx.x, + gridDim.x, ...). The next unit's
+// batch row and extent are fetched one unit ahead, so the dependent global
+// load is off the critical path of the role that walks it.
+struct UnitIter {
+  long long j;
+  int vt, b, E;  // current unit
+  int nvt, nb, nE;  // next unit (nE = -1: none)
+  __device__ __forceinline__ void load_next(const FwdTcParams& p) {
+    const long long jn = j + gridDim.x;
+    nE = -1;
+    if (jn < p.num_units) {
+      decode_unit(jn, p, nvt, nb);
+      nE = __ldg(p.extent + nb);
+    }
+  }
+  __device__ __forceinline__ bool start(const FwdTcParams& p) {
+    j = blockIdx.x;
+    if (j >= p.num_units) return false;
+    decode_unit(j, p, vt, b);
+    E = __ldg(p.extent + b);
+    load_next(p);
+    return true;
+  }
+  __device__ __forceinline__ bool advance(const FwdTcParams& p) {
+    if (nE < 0) return false;
+    j += gridDim.x;
+    vt = nvt;
+    b = nb;
+    E = nE;
+    load_next(p);
+    return true;
+  }
+};
+
 struct Ctrl {
   uint32_t bar0;  // shared address of barrier 0
   volatile int* abort_flag;
@@ -155,10 +189,9 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
   uint32_t phase = 0;
   uint32_t issued_mask = 0, issued_parity = 0;
   bool ok = true;
-  for (long long j = blockIdx.x; j < p.num_units && ok; j += gridDim.x) {
-    int vt, b;
-    decode_unit(j, p, vt, b);
-    const int E = __ldg(p.extent + b);
+  UnitIter u;
+  for (bool more = u.start(p); more && ok; more = u.advance(p)) {
+    const int vt = u.vt, b = u.b, E = u.E;
     for (int s0 = 0; s0 < E && ok; s0 += kBN) {
       const int n16 = (min(kBN, E - s0) + 15) >> 4;  // hidden rows / 16
       const uint32_t bytes = static_cast<uint32_t>(kABytes + n16 * 16 * kRowBytes);
@@ -205,13 +238,12 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
   uint32_t tile = 0;
   bool ok = true;
   bool issued = false;
-  for (long long j = blockIdx.x; j < p.num_units && ok; j += gridDim.x) {
-    int vt, b;
-    decode_unit(j, p, vt, b);
-    const int E = __ldg(p.extent + b);
+  UnitIter u;
+  for (bool more = u.start(p); more && ok; more = u.advance(p)) {
+    const int E = u.E;
     for (int s0 = 0; s0 < E; s0 += kBN) {
-      const int acc = tile & 1;
-      const uint32_t aph = (tile >> 1) & 1;
+      const int acc = tile % kNumAcc;
+      const uint32_t aph = (tile / kNumAcc) & 1;
       if (!mbar_wait_bounded_warp(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
                                   SPARTON_DEV_TIMEOUT_MMA)) {
         ok = false;
@@ -289,11 +321,10 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
   const int row = quad * 32 + lane;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
   uint32_t tile = 0;
-  for (long long j = blockIdx.x; j < p.num_units; j += gridDim.x) {
-    int vt, b;
-    decode_unit(j, p, vt, b);
-    const int E = __ldg(p.extent + b);
-    const int v = vt * kBM + row;
+  UnitIter u;
+  for (bool more = u.start(p); more; more = u.advance(p)) {
+    const int b = u.b, E = u.E;
+    const int v = u.vt * kBM + row;
     const uint32_t* bits_row = p.bits + static_cast<size_t>(b) * p.S32;
     const float bias = (p.bias != nullptr && v < p.V)
                            ? to_float<T>(static_cast<const T*>(p.bias)[v])
@@ -306,8 +337,8 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
       const int w0 = s0 >> 5;
       const uint32_t words =
           (lane < kTileWords && w0 + lane < p.S32) ? __ldg(bits_row + w0 + lane) : 0u;
-      const int acc = tile & 1;
-      const uint32_t aph = (tile >> 1) & 1;
+      const int acc = tile % kNumAcc;
+      const uint32_t aph = (tile / kNumAcc) & 1;
       // The whole warp leaves together (the TMEM loads below are warp-wide),
       // even if a wait gave up in only some of its lanes.
       const bool got = mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
