@@ -16,6 +16,9 @@
 //                        order: the B entries of each vocab id, contiguous.
 //   K3 gather_kernel<0>  one warp per (b, s) row: dH[b,s,:] = sum over its
 //                        bucket of g' * W[v,:] (W rows gathered, fp32 sums).
+//                        Persistent warps claim rows from a counter in the
+//                        workspace, position-major, so uneven buckets and the
+//                        empty rows past each sequence's end balance out.
 //   K4 gather_kernel<1>  one warp per vocab id: dW[v,:] = sum over b of
 //                        g' * H[b*S + idx[b,v], :] (neighbouring vocab ids share
 //                        H[b] rows in L1); db[v] is the sum of the same g'.
@@ -23,6 +26,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
+
+#include <mutex>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -168,13 +173,17 @@ template <typename T>
 __global__ void __launch_bounds__(1024)
     bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
                     const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
-                    int* __restrict__ perm, float* __restrict__ gperm, unsigned int* status) {
+                    int* __restrict__ perm, float* __restrict__ gperm, unsigned int* status,
+                    unsigned int* row_counter) {
   extern __shared__ int cnt[];  // [nw][S]
   __shared__ int scan_tmp[33];
   const int b = blockIdx.x;
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (b == 0 && threadIdx.x == 0) *status = 0u;
+  if (b == 0 && threadIdx.x == 0) {
+    *status = 0u;
+    *row_counter = 0u;
+  }
   for (int i = threadIdx.x; i < nw * S; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
 
@@ -315,20 +324,20 @@ constexpr int kGWarps = 8;
 constexpr int kGUnroll = 4;
 
 template <typename T, typename O, int NC, int kMode>
-__global__ void __launch_bounds__(kGWarps * 32)
-    gather_kernel(const T* __restrict__ src, int B, int S, int D, int V, const int* __restrict__ offs,
-                  const int* __restrict__ ent_row, const float* __restrict__ ent_coef, int n_rows,
-                  O* __restrict__ out, O* __restrict__ out_sum) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kGWarps + warp;
-  if (r >= n_rows) return;
-  int e0, e1;
+__device__ __forceinline__ void gather_row(const T* __restrict__ src, int B, int S, int D, int V,
+                                           const int* __restrict__ offs,
+                                           const int* __restrict__ ent_row,
+                                           const float* __restrict__ ent_coef, int q,
+                                           O* __restrict__ out, O* __restrict__ out_sum, int lane) {
+  int r, e0, e1;
   if (kMode == 0) {
-    const int b = r / S, s = r - (r / S) * S;
+    const int s = q / B, b = q - (q / B) * B;
+    r = b * S + s;
     const int* o = offs + static_cast<size_t>(b) * (S + 1);
     e0 = b * V + __ldg(o + s);
     e1 = b * V + __ldg(o + s + 1);
   } else {
+    r = q;
     e0 = r * B;
     e1 = e0 + B;
   }
@@ -387,6 +396,33 @@ __global__ void __launch_bounds__(kGWarps * 32)
   }
 }
 
+template <typename T, typename O, int NC, int kMode>
+__global__ void __launch_bounds__(kGWarps * 32)
+    gather_kernel(const T* __restrict__ src, int B, int S, int D, int V, const int* __restrict__ offs,
+                  const int* __restrict__ ent_row, const float* __restrict__ ent_coef, int n_rows,
+                  O* __restrict__ out, O* __restrict__ out_sum, unsigned int* row_counter) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (kMode == 0) {
+    // dH: persistent warps claim rows q = 0, 1, ... from the workspace counter
+    // (the next claim is issued before the current row is gathered). Rows are
+    // position-major (q -> s = q / B, b = q % B): the heavy rows come first
+    // and the empty rows past each sequence's end last.
+    int q = 0;
+    if (lane == 0) q = static_cast<int>(atomicAdd(row_counter, 1u));
+    q = __shfl_sync(0xFFFFFFFFu, q, 0);
+    while (q < n_rows) {
+      int qn = 0;
+      if (lane == 0) qn = static_cast<int>(atomicAdd(row_counter, 1u));
+      gather_row<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, q, out, out_sum, lane);
+      q = __shfl_sync(0xFFFFFFFFu, qn, 0);
+    }
+  } else {
+    const int r = blockIdx.x * kGWarps + warp;
+    if (r < n_rows)
+      gather_row<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, out, out_sum, lane);
+  }
+}
+
 template <typename T, typename O>
 __global__ void __launch_bounds__(256) db_kernel(const T* __restrict__ g, const T* __restrict__ reps,
                                                  int B, int V, O* __restrict__ db) {
@@ -419,39 +455,75 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
   }
   bwd_sort_kernel<T><<<B, nw * 32, smem, stream>>>(static_cast<const T*>(grad_reps),
                                                    static_cast<const T*>(reps), idx, S, V,
-                                                   ws.offs, ws.perm, ws.gperm, ws.status);
+                                                   ws.offs, ws.perm, ws.gperm, ws.status,
+                                                   ws.row_counter);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
   return SPARTON_OK;
 }
 
-template <typename T, typename O, int kMode>
-int launch_gather(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
-                  const float* ent_coef, int n_rows, O* out, O* out_sum, cudaStream_t stream) {
-  const unsigned grid = static_cast<unsigned>((n_rows + kGWarps - 1) / kGWarps);
+// Launches one gather_kernel instantiation with a persistent grid: resident
+// CTAs per SM (occupancy API, cached per device) x SMs, capped by the rows.
+template <typename T, typename O, int NC, int kMode>
+int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
+                     const float* ent_coef, int n_rows, O* out, O* out_sum,
+                     unsigned int* row_counter, cudaStream_t stream) {
+  static std::mutex mu;
+  static int per_sm[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int block = kGWarps * 32;
-  if (D <= 256)
-    gather_kernel<T, O, 1, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
-                                                              ent_coef, n_rows, out, out_sum);
-  else if (D <= 512)
-    gather_kernel<T, O, 2, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
-                                                              ent_coef, n_rows, out, out_sum);
-  else if (D <= 768)
-    gather_kernel<T, O, 3, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
-                                                              ent_coef, n_rows, out, out_sum);
-  else
-    gather_kernel<T, O, 4, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
-                                                              ent_coef, n_rows, out, out_sum);
-  const cudaError_t e = cudaGetLastError();
+  int bps = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    bps = dev < 64 ? per_sm[dev] : 0;
+    if (bps == 0) {
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, gather_kernel<T, O, NC, kMode>,
+                                                        block, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      if (bps < 1) bps = 1;
+      if (dev < 64) per_sm[dev] = bps;
+    }
+  }
+  // dH rows carry very different amounts of work (bucket sizes, empty rows past
+  // each sequence's end): persistent CTAs that claim rows dynamically.
+  // dW rows all carry B entries: one CTA per kGWarps rows, balanced by the
+  // hardware block scheduler.
+  const long long need = (static_cast<long long>(n_rows) + kGWarps - 1) / kGWarps;
+  const long long cap = kMode == 0 ? static_cast<long long>(bps) * device_sm_count() : need;
+  const unsigned grid = static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
+  gather_kernel<T, O, NC, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
+                                                            ent_coef, n_rows, out, out_sum,
+                                                            row_counter);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gather_kernel launch");
   return SPARTON_OK;
+}
+
+template <typename T, typename O, int kMode>
+int launch_gather(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
+                  const float* ent_coef, int n_rows, O* out, O* out_sum,
+                  unsigned int* row_counter, cudaStream_t stream) {
+  if (D <= 256)
+    return launch_gather_nc<T, O, 1, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
+                                            out_sum, row_counter, stream);
+  if (D <= 512)
+    return launch_gather_nc<T, O, 2, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
+                                            out_sum, row_counter, stream);
+  if (D <= 768)
+    return launch_gather_nc<T, O, 3, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
+                                            out_sum, row_counter, stream);
+  return launch_gather_nc<T, O, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
+                                          out_sum, row_counter, stream);
 }
 
 template <typename T, typename O>
 int launch_dh(const void* weight, int B, int S, int D, int V, void* d_hidden,
               const BwdWorkspace& ws, cudaStream_t stream) {
   return launch_gather<T, O, 0>(static_cast<const T*>(weight), B, S, D, V, ws.offs, ws.perm,
-                                ws.gperm, B * S, static_cast<O*>(d_hidden), nullptr, stream);
+                                ws.gperm, B * S, static_cast<O*>(d_hidden), nullptr,
+                                ws.row_counter, stream);
 }
 
 template <typename T, typename O>
@@ -466,7 +538,7 @@ int launch_dw(const void* grad_reps, const void* reps, const int32_t* idx, const
   if (e != cudaSuccess) return cuda_fail(e, "dw_list_kernel launch");
   return launch_gather<T, O, 1>(static_cast<const T*>(hidden), B, S, D, V, nullptr, ws.wrow,
                                 ws.wcoef, V, static_cast<O*>(d_weight), static_cast<O*>(d_bias),
-                                stream);
+                                nullptr, stream);
 }
 
 template <typename T, typename OH, typename OP>

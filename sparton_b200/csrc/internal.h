@@ -59,7 +59,8 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
 }
 
 // ----------------------------------------------------------- backward workspace
-// [0,256)      header: u32 status
+// [0,256)      header: u32 status, u32 next dH row to claim (both zeroed by the
+//              sort kernel at the start of every backward)
 // offs         B x (S+1) int32   bucket start of every position (CSR by position)
 // perm         B x V int32       vocab ids grouped by argmax position
 // gperm        B x V float       g' of those entries, same order
@@ -67,6 +68,7 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
 // wcoef        V x B float       per vocab id: g' of every b (0 when reps is 0)
 struct BwdWorkspace {
   unsigned int* status;
+  unsigned int* row_counter;
   int* offs;
   int* perm;
   float* gperm;
@@ -83,6 +85,7 @@ inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t 
   BwdWorkspace w;
   char* base = static_cast<char*>(ws);
   w.status = reinterpret_cast<unsigned int*>(base);
+  w.row_counter = reinterpret_cast<unsigned int*>(base) + 1;
   size_t off = 256;
   w.offs = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B * (S + 1)) * 4);
