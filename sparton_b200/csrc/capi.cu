@@ -21,10 +21,13 @@ int check_sizes(int64_t B, int64_t S, int64_t D, int64_t V) {
   if (B < 0 || S < 0 || D < 0 || V < 0)
     return fail(SPARTON_ERR_INVALID_ARGUMENT, "negative size (B=%lld S=%lld D=%lld V=%lld)",
                 (long long)B, (long long)S, (long long)D, (long long)V);
-  if (B > 65535 || S > (1 << 24) || D > (1 << 16) || V > (1 << 28) || B * S > (1ll << 31) - 1 ||
-      B * V > (1ll << 31) - 1)
+  // B * round16(S): the forward's packed position stream (one column per
+  // position, rows rounded up to 16) is indexed with 32-bit integers.
+  if (B > 65535 || S > (1 << 24) || D > (1 << 16) || V > (1 << 28) ||
+      B * ((S + 15) / 16 * 16) > (1ll << 31) - 1 || B * V > (1ll << 31) - 1)
     return fail(SPARTON_ERR_UNSUPPORTED,
-                "sizes out of range (B=%lld S=%lld D=%lld V=%lld; need B<=65535, B*S and B*V < 2^31)",
+                "sizes out of range (B=%lld S=%lld D=%lld V=%lld; need B<=65535, B*round16(S) and "
+                "B*V < 2^31)",
                 (long long)B, (long long)S, (long long)D, (long long)V);
   if (D % 8 != 0)
     return fail(SPARTON_ERR_UNSUPPORTED, "hidden size D=%lld must be a multiple of 8", (long long)D);

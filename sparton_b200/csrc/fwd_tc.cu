@@ -8,36 +8,45 @@
 // Here one persistent kernel does all of it and [B,S,V] never exists.
 //
 // Orientation. The GEMM is computed transposed: the MMA's M dimension is the
-// vocabulary (128 rows of W per tile, one TMEM lane per vocab id) and N is the
-// token dimension (up to 256 positions of one batch row). A thread of the
-// epilogue therefore owns one vocab id and scans its own TMEM lane along the
-// sequence: the max / argmax over S needs no cross-thread reduction.
+// vocabulary (128 rows of W per tile, one TMEM lane per vocab id) and N runs
+// over positions. A thread of the epilogue owns one vocab id and scans its own
+// TMEM lane along the positions: the max / argmax needs no cross-thread
+// reduction.
 //
-// Work unit = (vocab tile of 128, batch row b). The unit covers positions
-// [0, E_b) in s-tiles of <= 256, where E_b is the last valid position + 1.
-// The MMA N of an s-tile is its width rounded up to 16, and the hidden rows
-// of one K step arrive in ONE TMA box of exactly that many rows (16 tensor
-// maps, boxes of 16, 32, ..., 256 rows), so padded positions cost nothing and
-// a stage is two TMA requests. Units go round-robin over the CTAs (CTA i
-// takes units i, i + grid, ...). Order: panels of `panel_b` batch rows whose
-// hidden states fit in L2; inside a panel, groups of `group_b` rows; inside a
-// group, vocab-tile-major. Every role of a CTA walks the same unit sequence,
-// so no unit ids pass between them.
+// Packed positions. The positions [0, round16(extent)) of consecutive batch
+// rows are laid end to end (pack_prepare_kernel in mask.cu; workspace layout
+// in internal.h) and cut into groups of whole rows, ~2048 packed columns each.
+// Work unit = (vocab tile of 128, group). A unit is processed as tiles of 256
+// packed columns, so almost every MMA has N = 256 whatever the row lengths:
+// an MMA's cost has a large part that does not depend on N, and rows of ~150
+// positions one MMA tile each ran at ~60% of the 256-column rate. A tile holds
+// pieces of up to 16 rows; the producer loads each piece with ONE TMA box of
+// exactly its length (16 tensor maps, boxes of 16, 32, ..., 256 rows; pieces
+// start at 1024-byte aligned shared offsets, so the 128-byte swizzle matches
+// that of a single box). A tile's pieces are worked out once, one per lane of
+// the producer warp (from the group's list of rows with columns), and each
+// lane issues its own box. The epilogue follows the row boundaries through a
+// bitmap of row starts and carries a row's running max across tiles.
+//
+// Units go round-robin over the CTAs (CTA i takes units i, i + grid, ...), in
+// panel order: panels of groups whose hidden states fit in L2, vocab-tile-major
+// inside a panel. Every role of a CTA walks the same unit sequence, so no unit
+// ids pass between them. The number of groups is read from the workspace.
 //
 // Warp roles (192 threads, one CTA per SM):
-//   warp 0    TMA producer: W tile [128 x 64] + hidden tile [N x 64] per
+//   warp 0    TMA producer: W tile [128 x 64] + packed hidden tile [N x 64] per
 //             stage, 4 stages, 128-byte swizzle.
 //   warp 1    TMEM owner + MMA issuer: tcgen05.mma kind::f16, fp32 accumulator
-//             in TMEM, two 256-column accumulators (MMA of the next s-tile
+//             in TMEM, two 256-column accumulators (MMA of the next tile
 //             overlaps the epilogue of the previous one).
 //   Warps 0 and 1 run their loops with all 32 lanes and issue each TMA copy,
 //   MMA and commit from one elected lane (ptx.cuh elect_one).
 //   warps 2-5 epilogue: tcgen05.ld 32 columns at a time (the next chunk's load
 //             in flight while one is scanned), masked running max and
 //             first-index argmax over positions (strict >, as upstream
-//             :150-156), then bias, relu, log1p and the stores of reps / idx.
-//             The s-tile's mask words and the unit's bias are fetched before
-//             the wait for the accumulator, off the critical path.
+//             :150-156); at the end of each row: bias, relu, log1p and the
+//             stores of reps / idx. The tile's bitmap words and the unit's bias
+//             are fetched before the wait for the accumulator.
 //
 // Every wait is bounded (ptx.cuh); on timeout the CTA records a status code,
 // drains its in-flight TMA copies and MMAs, frees TMEM and exits.
@@ -55,7 +64,7 @@ namespace sparton {
 namespace {
 
 constexpr int kBM = 128;        // vocab rows per tile = MMA M = TMEM lanes
-constexpr int kBN = 256;        // max positions per s-tile = MMA N
+constexpr int kBN = 256;        // packed columns per tile = max MMA N
 constexpr int kBK = 64;         // K elements per stage: 128-byte rows
 constexpr int kStages = 4;      // TMA -> MMA pipeline depth
 constexpr int kRowBytes = kBK * 2;
@@ -67,9 +76,7 @@ constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kNumAcc * kBN;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-constexpr int kTileWords = kBN / 32;  // mask words per s-tile
-// Batch rows per unit group inside an L2 panel (0: the whole panel).
-constexpr int kRowGroup = 0;
+constexpr int kTileWords = kBN / 32;  // bitmap words per tile
 
 // Barrier indices inside the barrier block.
 constexpr int kBarFull = 0;
@@ -94,12 +101,17 @@ struct FwdTcParams {
   int B, S, D, V;
   int num_vtiles;
   int num_kblocks;
-  int panel_b;
-  int group_b;
-  long long num_units;
-  const uint32_t* bits;
-  int S32;
-  const int* extent;
+  int panel_g;  // groups per L2 panel
+  const unsigned int* num_groups;
+  const int* pcol;
+  const int* plen;
+  const int* gstart;
+  const int* gcols;
+  const int* gword;
+  const int* prows;
+  const int* gnz;
+  const uint32_t* pvalid;
+  const uint32_t* prow;
   const void* bias;
   void* reps;
   int32_t* idx;
@@ -127,51 +139,47 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
   return __float2half_rn(x);
 }
 
-__device__ __forceinline__ void decode_unit(long long j, const FwdTcParams& p, int& vt, int& b) {
-  const long long per_panel = static_cast<long long>(p.num_vtiles) * p.panel_b;
-  const long long panel = j / per_panel;
-  const long long r = j - panel * per_panel;
-  const int b0 = static_cast<int>(panel * p.panel_b);
-  const int pb = min(p.panel_b, p.B - b0);
-  // Row groups of group_b rows (the last may be shorter); every group before
-  // the one holding r is full.
-  const long long per_group = static_cast<long long>(p.num_vtiles) * p.group_b;
-  const int g = static_cast<int>(r / per_group);
-  const int rr = static_cast<int>(r - g * per_group);
-  const int gb = min(p.group_b, pb - g * p.group_b);
-  vt = rr / gb;
-  b = b0 + g * p.group_b + rr % gb;
-}
-
-// Walks the units of this CTA (blockIdx.x, + gridDim.x, ...). The next unit's
-// batch row and extent are fetched one unit ahead, so the dependent global
-// load is off the critical path of the role that walks it.
+// Walks the units (vocab tile, group) of this CTA: blockIdx.x, + gridDim.x, ...
+// The next unit's group columns are fetched one unit ahead.
 struct UnitIter {
-  long long j;
-  int vt, b, E;  // current unit
-  int nvt, nb, nE;  // next unit (nE = -1: none)
+  long long j, num_units;
+  int G;
+  int vt, g, cols;     // current unit
+  int nvt, ng, ncols;  // next unit (ncols = -1: none)
+  __device__ __forceinline__ void decode(long long u, const FwdTcParams& p, int& vt_,
+                                         int& g_) const {
+    const long long per_panel = static_cast<long long>(p.num_vtiles) * p.panel_g;
+    const long long panel = u / per_panel;
+    const int r = static_cast<int>(u - panel * per_panel);
+    const int g0 = static_cast<int>(panel) * p.panel_g;
+    const int pg = min(p.panel_g, G - g0);
+    vt_ = r / pg;
+    g_ = g0 + r % pg;
+  }
   __device__ __forceinline__ void load_next(const FwdTcParams& p) {
     const long long jn = j + gridDim.x;
-    nE = -1;
-    if (jn < p.num_units) {
-      decode_unit(jn, p, nvt, nb);
-      nE = __ldg(p.extent + nb);
+    ncols = -1;
+    if (jn < num_units) {
+      decode(jn, p, nvt, ng);
+      ncols = __ldg(p.gcols + ng);
     }
   }
   __device__ __forceinline__ bool start(const FwdTcParams& p) {
+    G = static_cast<int>(*p.num_groups);
+    num_units = static_cast<long long>(p.num_vtiles) * G;
     j = blockIdx.x;
-    if (j >= p.num_units) return false;
-    decode_unit(j, p, vt, b);
-    E = __ldg(p.extent + b);
+    if (j >= num_units) return false;
+    decode(j, p, vt, g);
+    cols = __ldg(p.gcols + g);
     load_next(p);
     return true;
   }
   __device__ __forceinline__ bool advance(const FwdTcParams& p) {
-    if (nE < 0) return false;
+    if (ncols < 0) return false;
     j += gridDim.x;
     vt = nvt;
-    b = nb;
-    E = nE;
+    g = ng;
+    cols = ncols;
     load_next(p);
     return true;
   }
@@ -189,27 +197,48 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
   uint32_t phase = 0;
   uint32_t issued_mask = 0, issued_parity = 0;
   bool ok = true;
+  const int lane = threadIdx.x & 31;
   UnitIter u;
   for (bool more = u.start(p); more && ok; more = u.advance(p)) {
-    const int vt = u.vt, b = u.b, E = u.E;
-    for (int s0 = 0; s0 < E && ok; s0 += kBN) {
-      const int n16 = (min(kBN, E - s0) + 15) >> 4;  // hidden rows / 16
-      const uint32_t bytes = static_cast<uint32_t>(kABytes + n16 * 16 * kRowBytes);
-      const CUtensorMap* map = tmH + (n16 - 1);
-      const int row0 = b * p.S + s0;
+    // k0: entry in prows of the first row that reaches into the current tile.
+    int k0 = __ldg(p.gnz + u.g);
+    const int k_end = __ldg(p.gnz + u.g + 1);
+    for (int t0 = 0; t0 < u.cols && ok; t0 += kBN) {
+      const int n = min(kBN, u.cols - t0);  // a multiple of 16
+      const int t1 = t0 + n;
+      // Lane i describes piece i of the tile: row prows[k0 + i] clipped to
+      // [t0, t1). Pieces are >= 16 columns, so a tile has at most 16.
+      bool has_piece = false;
+      uint32_t dst_off = 0;
+      int grow = 0, map_i = 0;
+      bool ends_here = false;
+      if (lane < kBN / 16 && k0 + lane < k_end) {
+        const int b = __ldg(p.prows + k0 + lane);
+        const int c0 = __ldg(p.pcol + b), c1 = c0 + __ldg(p.plen + b);
+        const int s0 = max(c0, t0), s1 = min(c1, t1);
+        has_piece = s0 < s1;
+        ends_here = has_piece && c1 <= t1;
+        dst_off = static_cast<uint32_t>(kABytes + (s0 - t0) * kRowBytes);
+        grow = b * p.S + (s0 - c0);
+        map_i = (s1 - s0) / 16 - 1;
+      }
+      k0 += __popc(__ballot_sync(0xFFFFFFFFu, ends_here));
+      const uint32_t bytes = static_cast<uint32_t>(kABytes + n * kRowBytes);
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
         if (!mbar_wait_bounded_warp(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
                                     SPARTON_DEV_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
-        if (elect_one()) {
-          const uint32_t full = c.bar(kBarFull + stage);
+        const uint32_t full = c.bar(kBarFull + stage);
+        const uint32_t a_dst = stage_base + stage * kStageBytes;
+        if (lane == 0) {
           mbar_arrive_expect_tx(full, bytes);
-          const uint32_t a_dst = stage_base + stage * kStageBytes;
-          tma_load_2d(a_dst, tmW, full, kb * kBK, vt * kBM);
-          tma_load_2d(a_dst + kABytes, map, full, kb * kBK, row0);
+          tma_load_2d(a_dst, tmW, full, kb * kBK, u.vt * kBM);
         }
+        __syncwarp();
+        // One box per row piece; the pieces tile [t0, t1) exactly.
+        if (has_piece) tma_load_2d(a_dst + dst_off, tmH + map_i, full, kb * kBK, grow);
         __syncwarp();
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -240,8 +269,7 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
   bool issued = false;
   UnitIter u;
   for (bool more = u.start(p); more && ok; more = u.advance(p)) {
-    const int E = u.E;
-    for (int s0 = 0; s0 < E; s0 += kBN) {
+    for (int t0 = 0; t0 < u.cols; t0 += kBN) {
       const int acc = tile % kNumAcc;
       const uint32_t aph = (tile / kNumAcc) & 1;
       if (!mbar_wait_bounded_warp(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
@@ -250,7 +278,7 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
         break;
       }
       tc_fence_after_sync();
-      const uint32_t n_mma = static_cast<uint32_t>((min(kBN, E - s0) + 15) & ~15);
+      const uint32_t n_mma = static_cast<uint32_t>(min(kBN, u.cols - t0));
       const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma);
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
@@ -291,8 +319,8 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
   }
 }
 
-// Folds 32 consecutive positions (one TMEM chunk, mask word `mw`, first
-// position `pos0`) into the running masked max / first argmax.
+// Folds the columns of one TMEM chunk selected by `mw` into the running masked
+// max / first argmax; column q of the chunk is position pos0 + q of the row.
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw, int pos0,
                                            float& best, int& best_idx) {
   if (mw == 0u) return;
@@ -314,6 +342,67 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw,
   }
 }
 
+// Per-thread state of the epilogue inside one unit: the current row and its
+// running max. Rows are visited in order; empty rows (no packed columns) are
+// written as the empty-row value when the walk passes them.
+template <typename T>
+struct RowWalk {
+  int b;         // current row (below the group's first row: none yet)
+  int nxt;       // the next row with columns (the group's end: none)
+  int kk;        // entry in prows after nxt
+  int k_end;     // end of the group's entries in prows
+  int g_end;
+  int row_base;  // packed column of the current row's position 0
+  float best;
+  int best_idx;
+  int v;
+  float bias;
+
+  __device__ __forceinline__ void store(const FwdTcParams& p, int row) const {
+    if (v < p.V) {
+      // max_s(x_s + bias) = max_s(x_s) + bias: the bias is added once, after the
+      // max. Upstream's initial value 0 (:112) is the `logit > 0` test.
+      const float logit = best + bias;
+      const bool pos = logit > 0.f;
+      const size_t o = static_cast<size_t>(row) * p.V + v;
+      static_cast<T*>(p.reps)[o] = from_float<T>(pos ? log1pf(logit) : 0.f);
+      p.idx[o] = pos ? best_idx : 0;
+    }
+  }
+  // Stores the current row (if any), then every (empty) row before `upto`.
+  __device__ __forceinline__ void finish_until(const FwdTcParams& p, int first_row, int upto) {
+    if (b >= first_row) store(p, b);
+    best = -INFINITY;
+    best_idx = 0;
+    for (int e = max(b + 1, first_row); e < upto; ++e) store(p, e);
+  }
+  // A row starts at packed column `col`: it is `nxt`, the next row with
+  // columns; the one after it is fetched now, for the next row start.
+  __device__ __forceinline__ void next_row(const FwdTcParams& p, int first_row, int col) {
+    finish_until(p, first_row, nxt);
+    b = nxt;
+    row_base = col;
+    nxt = kk < k_end ? __ldg(p.prows + kk) : g_end;
+    ++kk;
+  }
+};
+
+// One 32-column chunk at packed column cc: valid bits `mw`, row starts `rs`
+// (rows start at multiples of 16, so only bits 0 and 16 can be set).
+template <typename T>
+__device__ __forceinline__ void epi_chunk(const FwdTcParams& p, const uint32_t (&r)[32],
+                                          uint32_t mw, uint32_t rs, int cc, int first_row,
+                                          RowWalk<T>& w) {
+  if (rs & 1u) w.next_row(p, first_row, cc);
+  if (rs & 0x10000u) {
+    scan_chunk(r, mw & 0xFFFFu, cc - w.row_base, w.best, w.best_idx);
+    w.next_row(p, first_row, cc + 16);
+    scan_chunk(r, mw & 0xFFFF0000u, cc - w.row_base, w.best, w.best_idx);
+  } else {
+    scan_chunk(r, mw, cc - w.row_base, w.best, w.best_idx);
+  }
+}
+
 template <typename T>
 __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
                              int lane) {
@@ -323,20 +412,27 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
   uint32_t tile = 0;
   UnitIter u;
   for (bool more = u.start(p); more; more = u.advance(p)) {
-    const int b = u.b, E = u.E;
-    const int v = u.vt * kBM + row;
-    const uint32_t* bits_row = p.bits + static_cast<size_t>(b) * p.S32;
-    const float bias = (p.bias != nullptr && v < p.V)
-                           ? to_float<T>(static_cast<const T*>(p.bias)[v])
-                           : 0.f;
-    float best = -INFINITY;
-    int best_idx = 0;
+    const int g_begin = __ldg(p.gstart + u.g), g_end = __ldg(p.gstart + u.g + 1);
+    const int w_begin = __ldg(p.gword + u.g);
+    RowWalk<T> w;
+    w.b = g_begin - 1;
+    w.kk = __ldg(p.gnz + u.g);
+    w.k_end = __ldg(p.gnz + u.g + 1);
+    w.g_end = g_end;
+    w.nxt = w.kk < w.k_end ? __ldg(p.prows + w.kk) : g_end;
+    ++w.kk;
+    w.row_base = 0;
+    w.best = -INFINITY;
+    w.best_idx = 0;
+    w.v = u.vt * kBM + row;
+    w.bias = (p.bias != nullptr && w.v < p.V) ? to_float<T>(static_cast<const T*>(p.bias)[w.v])
+                                               : 0.f;
     bool ok = true;
-    for (int s0 = 0; s0 < E; s0 += kBN) {
-      // Lane i holds mask word i of this s-tile (positions s0 + 32i ...).
-      const int w0 = s0 >> 5;
-      const uint32_t words =
-          (lane < kTileWords && w0 + lane < p.S32) ? __ldg(bits_row + w0 + lane) : 0u;
+    for (int t0 = 0; t0 < u.cols; t0 += kBN) {
+      // Lane i holds bitmap word i of this tile (packed columns t0 + 32i ...).
+      const int wi = w_begin + (t0 >> 5) + lane;
+      const uint32_t vwords = lane < kTileWords ? __ldg(p.pvalid + wi) : 0u;
+      const uint32_t swords = lane < kTileWords ? __ldg(p.prow + wi) : 0u;
       const int acc = tile % kNumAcc;
       const uint32_t aph = (tile / kNumAcc) & 1;
       // The whole warp leaves together (the TMEM loads below are warp-wide),
@@ -348,19 +444,20 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
         break;
       }
       tc_fence_after_sync();
-      const int nch = (min(kBN, E - s0) + 31) >> 5;
+      const int nch = (min(kBN, u.cols - t0) + 31) >> 5;
       const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * kBN);
       uint32_t ra[32], rb[32];
       tmem_ld_32x32b_x32(taddr, ra);
       for (int ch = 0; ch < nch; ch += 2) {
         tmem_ld_wait(ra);
         if (ch + 1 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 1)), rb);
-        scan_chunk(ra, __shfl_sync(0xFFFFFFFFu, words, ch), s0 + 32 * ch, best, best_idx);
+        epi_chunk<T>(p, ra, __shfl_sync(0xFFFFFFFFu, vwords, ch),
+                     __shfl_sync(0xFFFFFFFFu, swords, ch), t0 + 32 * ch, g_begin, w);
         if (ch + 1 < nch) {
           tmem_ld_wait(rb);
           if (ch + 2 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 2)), ra);
-          scan_chunk(rb, __shfl_sync(0xFFFFFFFFu, words, ch + 1), s0 + 32 * (ch + 1), best,
-                     best_idx);
+          epi_chunk<T>(p, rb, __shfl_sync(0xFFFFFFFFu, vwords, ch + 1),
+                       __shfl_sync(0xFFFFFFFFu, swords, ch + 1), t0 + 32 * (ch + 1), g_begin, w);
         }
       }
       tc_fence_before_sync();
@@ -369,15 +466,7 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
       ++tile;
     }
     if (!ok) break;
-    if (v < p.V) {
-      // max_s(x_s + bias) = max_s(x_s) + bias: the bias is added once, after the
-      // max. Upstream's initial value 0 (:112) is the `logit > 0` test.
-      const float logit = best + bias;
-      const bool pos = logit > 0.f;
-      const size_t o = static_cast<size_t>(b) * p.V + v;
-      static_cast<T*>(p.reps)[o] = from_float<T>(pos ? log1pf(logit) : 0.f);
-      p.idx[o] = pos ? best_idx : 0;
-    }
+    w.finish_until(p, g_begin, g_end);
   }
 }
 
@@ -472,17 +561,23 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
   p.V = V;
   p.num_vtiles = (V + kBM - 1) / kBM;
   p.num_kblocks = (D + kBK - 1) / kBK;
-  // Panel of batch rows whose hidden states (S*D*2 bytes each) fit in ~48 MB of L2.
-  const long long row_bytes = static_cast<long long>(S) * D * 2;
-  long long pb = (48ll << 20) / (row_bytes > 0 ? row_bytes : 1);
-  if (pb < 1) pb = 1;
-  if (pb > B) pb = B;
-  p.panel_b = static_cast<int>(pb);
-  p.group_b = (kRowGroup > 0 && kRowGroup < p.panel_b) ? kRowGroup : p.panel_b;
-  p.num_units = static_cast<long long>(p.num_vtiles) * B;
-  p.bits = ws.bits;
-  p.S32 = ws.S32;
-  p.extent = ws.extent;
+  // Panel of groups whose hidden states (a group holds up to ~2 * group_cols
+  // packed columns of D * 2 bytes) fit in ~48 MB of L2.
+  const long long group_bytes = 2 * fwd_group_cols(S) * static_cast<long long>(D) * 2;
+  long long pg = (48ll << 20) / (group_bytes > 0 ? group_bytes : 1);
+  if (pg < 1) pg = 1;
+  if (pg > B) pg = B;
+  p.panel_g = static_cast<int>(pg);
+  p.num_groups = ws.num_groups;
+  p.pcol = ws.pcol;
+  p.plen = ws.plen;
+  p.gstart = ws.gstart;
+  p.gcols = ws.gcols;
+  p.gword = ws.gword;
+  p.prows = ws.prows;
+  p.gnz = ws.gnz;
+  p.pvalid = ws.pvalid;
+  p.prow = ws.prow;
   p.bias = bias;
   p.reps = reps;
   p.idx = idx;
@@ -502,7 +597,10 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
       attr_done[dev] = true;
     }
   }
-  const long long grid_ll = p.num_units < device_sm_count() ? p.num_units : device_sm_count();
+  // The number of units (vocab tiles x groups) is known on the device only;
+  // there are at most num_vtiles * B of them.
+  const long long max_units = static_cast<long long>(p.num_vtiles) * B;
+  const long long grid_ll = max_units < device_sm_count() ? max_units : device_sm_count();
   const unsigned grid = static_cast<unsigned>(grid_ll > 0 ? grid_ll : 1);
   fwd_tc_kernel<T, kFmt><<<grid, kThreads, kSmemBytes, stream>>>(tmW, tmH, p);
   e = cudaGetLastError();
