@@ -347,7 +347,9 @@ def main(argv=None) -> int:
     step_ms = max_over_ranks(sum(a.elapsed_time(e) for a, e in step_ev) / args.steps)
     kern_ms = sum(a.elapsed_time(e) for a, e in kern_ev) / args.steps
     kern_ms_max = max_over_ranks(kern_ms)
-    launches_per_step = 2 + (4 if bd is not None else 3)
+    # mask_prepare + pack_prepare + forward; backward: sort, dH gather, dW list,
+    # dW gather (db, when there is a bias, is summed inside the dW gather).
+    launches_per_step = 3 + 4
 
     # ------------------------------------------------------------ end to end
     e2e_ms = None
