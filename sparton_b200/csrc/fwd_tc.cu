@@ -13,11 +13,17 @@
 // TMEM lane along the positions: the max / argmax needs no cross-thread
 // reduction.
 //
-// Packed positions. The positions [0, round16(extent)) of consecutive batch
-// rows are laid end to end (pack_prepare_kernel in mask.cu; workspace layout
-// in internal.h) and cut into groups of whole rows, ~2048 packed columns each.
-// Work unit = (vocab tile of 128, group). A unit is processed as tiles of 256
-// packed columns, so almost every MMA has N = 256 whatever the row lengths:
+// Packed positions. The positions [0, round16(extent)) of all batch rows are
+// laid end to end in one stream of T packed columns (pack_prepare_kernel in
+// mask.cu; workspace layout in internal.h). The kernel cuts the rows into G
+// groups by the packed column at which each row starts (group g: rows
+// starting in [g*T/G, (g+1)*T/G)); a work unit is (vocab tile of 128, group).
+// G is chosen on the device from T, the vocab tile count and the grid, so that
+// the units spread evenly over the CTAs: it minimises
+//   ceil(units / CTAs) * (tiles per unit + 1/2)
+// (the 1/2 stands for the part-filled last tile of a unit). Every CTA computes
+// the same G. A unit is processed as tiles of 256 packed columns, so almost
+// every MMA has N = 256 whatever the row lengths:
 // an MMA's cost has a large part that does not depend on N, and rows of ~150
 // positions one MMA tile each ran at ~60% of the 256-column rate. A tile holds
 // pieces of up to 16 rows; the producer loads each piece with ONE TMA box of
@@ -31,7 +37,7 @@
 // Units go round-robin over the CTAs (CTA i takes units i, i + grid, ...), in
 // panel order: panels of groups whose hidden states fit in L2, vocab-tile-major
 // inside a panel. Every role of a CTA walks the same unit sequence, so no unit
-// ids pass between them. The number of groups is read from the workspace.
+// ids pass between them.
 //
 // Warp roles (192 threads, one CTA per SM):
 //   warp 0    TMA producer: W tile [128 x 64] + packed hidden tile [N x 64] per
@@ -89,8 +95,10 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr int kCtrlOffset = kStages * kStageBytes;  // barriers, TMEM address, abort flag
 constexpr int kTmemHolderOffset = kCtrlOffset + kNumBars * 8;
 constexpr int kAbortOffset = kTmemHolderOffset + 4;
+constexpr int kPartOffset = kAbortOffset + 4;  // float[kThreads/32] + int[kThreads/32]
 constexpr int kCtrlBytes = 512;
-static_assert(kAbortOffset + 4 <= kCtrlOffset + kCtrlBytes, "control block overflow");
+static_assert(kPartOffset + 8 * (kThreads / 32) <= kCtrlOffset + kCtrlBytes,
+              "control block overflow");
 constexpr int kSmemBytes = kCtrlOffset + kCtrlBytes + 1024;  // + alignment slack
 
 struct alignas(64) HiddenMaps {
@@ -101,15 +109,11 @@ struct FwdTcParams {
   int B, S, D, V;
   int num_vtiles;
   int num_kblocks;
-  int panel_g;  // groups per L2 panel
-  const unsigned int* num_groups;
+  const unsigned int* total_cols;
   const int* pcol;
   const int* plen;
-  const int* gstart;
-  const int* gcols;
-  const int* gword;
+  const int* pnz;
   const int* prows;
-  const int* gnz;
   const uint32_t* pvalid;
   const uint32_t* prow;
   const void* bias;
@@ -139,48 +143,66 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
   return __float2half_rn(x);
 }
 
-// Walks the units (vocab tile, group) of this CTA: blockIdx.x, + gridDim.x, ...
-// The next unit's group columns are fetched one unit ahead.
+// How the rows are cut into groups for this launch (identical in every CTA).
+struct Partition {
+  int T;        // packed columns in total
+  int G;        // row groups
+  int panel_g;  // groups per L2 panel
+  long long num_units;
+};
+
+// First row whose packed start is >= x (B if none).
+__device__ __forceinline__ int first_row_from(const FwdTcParams& p, long long x) {
+  int lo = 0, hi = p.B;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(p.pcol + mid) < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+// One unit: vocab tile vt, rows [r0, r1), packed columns [c0, c1), entries
+// [k0, k1) of prows.
+struct Unit {
+  int vt, r0, r1, c0, c1, k0, k1;
+};
+
+// Walks the units of this CTA: blockIdx.x, + gridDim.x, ... The next unit is
+// located (binary searches over the row starts) one unit ahead.
 struct UnitIter {
-  long long j, num_units;
-  int G;
-  int vt, g, cols;     // current unit
-  int nvt, ng, ncols;  // next unit (ncols = -1: none)
-  __device__ __forceinline__ void decode(long long u, const FwdTcParams& p, int& vt_,
-                                         int& g_) const {
-    const long long per_panel = static_cast<long long>(p.num_vtiles) * p.panel_g;
+  long long j;
+  Unit cur, nxt;
+  bool has_next;
+  __device__ __forceinline__ void locate(long long u, const FwdTcParams& p, const Partition& q,
+                                         Unit& o) const {
+    const long long per_panel = static_cast<long long>(p.num_vtiles) * q.panel_g;
     const long long panel = u / per_panel;
     const int r = static_cast<int>(u - panel * per_panel);
-    const int g0 = static_cast<int>(panel) * p.panel_g;
-    const int pg = min(p.panel_g, G - g0);
-    vt_ = r / pg;
-    g_ = g0 + r % pg;
+    const int g0 = static_cast<int>(panel) * q.panel_g;
+    const int pg = min(q.panel_g, q.G - g0);
+    const int g = g0 + r % pg;
+    o.vt = r / pg;
+    o.r0 = g == 0 ? 0 : first_row_from(p, static_cast<long long>(g) * q.T / q.G);
+    o.r1 = g == q.G - 1 ? p.B : first_row_from(p, static_cast<long long>(g + 1) * q.T / q.G);
+    o.c0 = o.r0 < p.B ? __ldg(p.pcol + o.r0) : q.T;
+    o.c1 = o.r1 < p.B ? __ldg(p.pcol + o.r1) : q.T;
+    o.k0 = __ldg(p.pnz + o.r0);
+    o.k1 = __ldg(p.pnz + o.r1);
   }
-  __device__ __forceinline__ void load_next(const FwdTcParams& p) {
-    const long long jn = j + gridDim.x;
-    ncols = -1;
-    if (jn < num_units) {
-      decode(jn, p, nvt, ng);
-      ncols = __ldg(p.gcols + ng);
-    }
-  }
-  __device__ __forceinline__ bool start(const FwdTcParams& p) {
-    G = static_cast<int>(*p.num_groups);
-    num_units = static_cast<long long>(p.num_vtiles) * G;
+  __device__ __forceinline__ bool start(const FwdTcParams& p, const Partition& q) {
     j = blockIdx.x;
-    if (j >= num_units) return false;
-    decode(j, p, vt, g);
-    cols = __ldg(p.gcols + g);
-    load_next(p);
+    if (j >= q.num_units) return false;
+    locate(j, p, q, cur);
+    has_next = j + gridDim.x < q.num_units;
+    if (has_next) locate(j + gridDim.x, p, q, nxt);
     return true;
   }
-  __device__ __forceinline__ bool advance(const FwdTcParams& p) {
-    if (ncols < 0) return false;
+  __device__ __forceinline__ bool advance(const FwdTcParams& p, const Partition& q) {
+    if (!has_next) return false;
     j += gridDim.x;
-    vt = nvt;
-    g = ng;
-    cols = ncols;
-    load_next(p);
+    cur = nxt;
+    has_next = j + gridDim.x < q.num_units;
+    if (has_next) locate(j + gridDim.x, p, q, nxt);
     return true;
   }
 };
@@ -191,20 +213,21 @@ struct Ctrl {
   __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * i; }
 };
 
-__device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const CUtensorMap* tmH,
-                             uint32_t stage_base, const Ctrl& c) {
+__device__ void run_producer(const FwdTcParams& p, const Partition& q, const CUtensorMap* tmW,
+                             const CUtensorMap* tmH, uint32_t stage_base, const Ctrl& c) {
   int stage = 0;
   uint32_t phase = 0;
   uint32_t issued_mask = 0, issued_parity = 0;
   bool ok = true;
   const int lane = threadIdx.x & 31;
   UnitIter u;
-  for (bool more = u.start(p); more && ok; more = u.advance(p)) {
+  for (bool more = u.start(p, q); more && ok; more = u.advance(p, q)) {
+    const Unit& un = u.cur;
     // k0: entry in prows of the first row that reaches into the current tile.
-    int k0 = __ldg(p.gnz + u.g);
-    const int k_end = __ldg(p.gnz + u.g + 1);
-    for (int t0 = 0; t0 < u.cols && ok; t0 += kBN) {
-      const int n = min(kBN, u.cols - t0);  // a multiple of 16
+    int k0 = un.k0;
+    const int k_end = un.k1;
+    for (int t0 = un.c0; t0 < un.c1 && ok; t0 += kBN) {
+      const int n = min(kBN, un.c1 - t0);  // a multiple of 16
       const int t1 = t0 + n;
       // Lane i describes piece i of the tile: row prows[k0 + i] clipped to
       // [t0, t1). Pieces are >= 16 columns, so a tile has at most 16.
@@ -234,7 +257,7 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
         const uint32_t a_dst = stage_base + stage * kStageBytes;
         if (lane == 0) {
           mbar_arrive_expect_tx(full, bytes);
-          tma_load_2d(a_dst, tmW, full, kb * kBK, u.vt * kBM);
+          tma_load_2d(a_dst, tmW, full, kb * kBK, un.vt * kBM);
         }
         __syncwarp();
         // One box per row piece; the pieces tile [t0, t1) exactly.
@@ -260,16 +283,17 @@ __device__ void run_producer(const FwdTcParams& p, const CUtensorMap* tmW, const
 }
 
 template <uint32_t kFmt>
-__device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem_base,
-                        const Ctrl& c) {
+__device__ void run_mma(const FwdTcParams& p, const Partition& q, uint32_t stage_base,
+                        uint32_t tmem_base, const Ctrl& c) {
   int stage = 0;
   uint32_t phase = 0;
   uint32_t tile = 0;
   bool ok = true;
   bool issued = false;
   UnitIter u;
-  for (bool more = u.start(p); more && ok; more = u.advance(p)) {
-    for (int t0 = 0; t0 < u.cols; t0 += kBN) {
+  for (bool more = u.start(p, q); more && ok; more = u.advance(p, q)) {
+    const Unit& un = u.cur;
+    for (int t0 = un.c0; t0 < un.c1; t0 += kBN) {
       const int acc = tile % kNumAcc;
       const uint32_t aph = (tile / kNumAcc) & 1;
       if (!mbar_wait_bounded_warp(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
@@ -278,7 +302,7 @@ __device__ void run_mma(const FwdTcParams& p, uint32_t stage_base, uint32_t tmem
         break;
       }
       tc_fence_after_sync();
-      const uint32_t n_mma = static_cast<uint32_t>(min(kBN, u.cols - t0));
+      const uint32_t n_mma = static_cast<uint32_t>(min(kBN, un.c1 - t0));
       const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma);
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
       for (int kb = 0; kb < p.num_kblocks; ++kb) {
@@ -387,6 +411,17 @@ struct RowWalk {
   }
 };
 
+// Bits of chunk ch of a tile whose first column sits `sh` bits into the word
+// held by lane 0 (lane i holds the tile's word i), limited to the columns
+// before the unit's end (`left` columns remain from the chunk's start): the
+// stream goes on with the next unit's rows.
+__device__ __forceinline__ uint32_t chunk_bits(uint32_t words, int ch, int sh, int left) {
+  const uint32_t lo = __shfl_sync(0xFFFFFFFFu, words, ch);
+  const uint32_t hi = __shfl_sync(0xFFFFFFFFu, words, ch + 1);
+  const uint32_t lim = left >= 32 ? 0xFFFFFFFFu : ((1u << left) - 1u);
+  return __funnelshift_r(lo, hi, sh) & lim;
+}
+
 // One 32-column chunk at packed column cc: valid bits `mw`, row starts `rs`
 // (rows start at multiples of 16, so only bits 0 and 16 can be set).
 template <typename T>
@@ -404,35 +439,36 @@ __device__ __forceinline__ void epi_chunk(const FwdTcParams& p, const uint32_t (
 }
 
 template <typename T>
-__device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
-                             int lane) {
+__device__ void run_epilogue(const FwdTcParams& p, const Partition& q, uint32_t tmem_base,
+                             const Ctrl& c, int warp, int lane) {
   const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
   const int row = quad * 32 + lane;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
   uint32_t tile = 0;
   UnitIter u;
-  for (bool more = u.start(p); more; more = u.advance(p)) {
-    const int g_begin = __ldg(p.gstart + u.g), g_end = __ldg(p.gstart + u.g + 1);
-    const int w_begin = __ldg(p.gword + u.g);
+  for (bool more = u.start(p, q); more; more = u.advance(p, q)) {
+    const Unit& un = u.cur;
+    const int g_begin = un.r0, g_end = un.r1;
     RowWalk<T> w;
     w.b = g_begin - 1;
-    w.kk = __ldg(p.gnz + u.g);
-    w.k_end = __ldg(p.gnz + u.g + 1);
+    w.kk = un.k0;
+    w.k_end = un.k1;
     w.g_end = g_end;
     w.nxt = w.kk < w.k_end ? __ldg(p.prows + w.kk) : g_end;
     ++w.kk;
     w.row_base = 0;
     w.best = -INFINITY;
     w.best_idx = 0;
-    w.v = u.vt * kBM + row;
+    w.v = un.vt * kBM + row;
     w.bias = (p.bias != nullptr && w.v < p.V) ? to_float<T>(static_cast<const T*>(p.bias)[w.v])
                                                : 0.f;
     bool ok = true;
-    for (int t0 = 0; t0 < u.cols; t0 += kBN) {
-      // Lane i holds bitmap word i of this tile (packed columns t0 + 32i ...).
-      const int wi = w_begin + (t0 >> 5) + lane;
-      const uint32_t vwords = lane < kTileWords ? __ldg(p.pvalid + wi) : 0u;
-      const uint32_t swords = lane < kTileWords ? __ldg(p.prow + wi) : 0u;
+    for (int t0 = un.c0; t0 < un.c1; t0 += kBN) {
+      // Lane i holds bitmap word (t0 >> 5) + i; a tile starts at a multiple of
+      // 16, so chunk ch is a funnel shift of words ch and ch + 1.
+      const int wsh = t0 & 31;
+      const uint32_t vwords = lane <= kTileWords ? __ldg(p.pvalid + (t0 >> 5) + lane) : 0u;
+      const uint32_t swords = lane <= kTileWords ? __ldg(p.prow + (t0 >> 5) + lane) : 0u;
       const int acc = tile % kNumAcc;
       const uint32_t aph = (tile / kNumAcc) & 1;
       // The whole warp leaves together (the TMEM loads below are warp-wide),
@@ -444,20 +480,22 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
         break;
       }
       tc_fence_after_sync();
-      const int nch = (min(kBN, u.cols - t0) + 31) >> 5;
+      const int nch = (min(kBN, un.c1 - t0) + 31) >> 5;
       const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * kBN);
       uint32_t ra[32], rb[32];
       tmem_ld_32x32b_x32(taddr, ra);
       for (int ch = 0; ch < nch; ch += 2) {
         tmem_ld_wait(ra);
         if (ch + 1 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 1)), rb);
-        epi_chunk<T>(p, ra, __shfl_sync(0xFFFFFFFFu, vwords, ch),
-                     __shfl_sync(0xFFFFFFFFu, swords, ch), t0 + 32 * ch, g_begin, w);
+        const int left0 = un.c1 - (t0 + 32 * ch);
+        epi_chunk<T>(p, ra, chunk_bits(vwords, ch, wsh, left0),
+                     chunk_bits(swords, ch, wsh, left0), t0 + 32 * ch, g_begin, w);
         if (ch + 1 < nch) {
           tmem_ld_wait(rb);
           if (ch + 2 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 2)), ra);
-          epi_chunk<T>(p, rb, __shfl_sync(0xFFFFFFFFu, vwords, ch + 1),
-                       __shfl_sync(0xFFFFFFFFu, swords, ch + 1), t0 + 32 * (ch + 1), g_begin, w);
+          const int left1 = un.c1 - (t0 + 32 * (ch + 1));
+          epi_chunk<T>(p, rb, chunk_bits(vwords, ch + 1, wsh, left1),
+                       chunk_bits(swords, ch + 1, wsh, left1), t0 + 32 * (ch + 1), g_begin, w);
         }
       }
       tc_fence_before_sync();
@@ -468,6 +506,57 @@ __device__ void run_epilogue(const FwdTcParams& p, uint32_t tmem_base, const Ctr
     if (!ok) break;
     w.finish_until(p, g_begin, g_end);
   }
+}
+
+// Chooses G for this launch; all threads of the CTA take part and every CTA
+// gets the same answer. Candidate G = 1 .. min(B, 4 * grid); cost as in the
+// header comment; ties go to the smaller G.
+__device__ Partition choose_partition(const FwdTcParams& p, float* red_cost, int* red_g) {
+  Partition q;
+  q.T = static_cast<int>(*p.total_cols);
+  const int gmax = max(1, min(p.B, 4 * static_cast<int>(gridDim.x)));
+  float best = INFINITY;
+  int best_g = 1;
+  for (int g = threadIdx.x + 1; g <= gmax; g += blockDim.x) {
+    const long long units = static_cast<long long>(p.num_vtiles) * g;
+    const long long rounds = (units + gridDim.x - 1) / gridDim.x;
+    const float cost = static_cast<float>(rounds) *
+                       (static_cast<float>(q.T) / (256.f * static_cast<float>(g)) + 0.5f);
+    if (cost < best) {
+      best = cost;
+      best_g = g;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oc = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int og = __shfl_xor_sync(0xFFFFFFFFu, best_g, o);
+    if (oc < best || (oc == best && og < best_g)) {
+      best = oc;
+      best_g = og;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_cost[warp] = best;
+    red_g[warp] = best_g;
+  }
+  __syncthreads();
+  best = red_cost[0];
+  best_g = red_g[0];
+  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+    if (red_cost[w] < best || (red_cost[w] == best && red_g[w] < best_g)) {
+      best = red_cost[w];
+      best_g = red_g[w];
+    }
+  }
+  q.G = best_g;
+  q.num_units = static_cast<long long>(p.num_vtiles) * q.G;
+  // Panel of groups whose hidden states (~T/G packed columns of D * 2 bytes
+  // each) fit in ~48 MB of L2.
+  const long long group_bytes =
+      (static_cast<long long>(q.T) / q.G + 256) * static_cast<long long>(p.D) * 2;
+  q.panel_g = static_cast<int>(max(1ll, min(static_cast<long long>(q.G), (48ll << 20) / group_bytes)));
+  return q;
 }
 
 template <typename T, uint32_t kFmt>
@@ -508,19 +597,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_addr(tmem_holder), kTmemCols);
     tmem_relinquish();
   }
+  const Partition q = choose_partition(p, reinterpret_cast<float*>(smem + kPartOffset),
+                                       reinterpret_cast<int*>(smem + kPartOffset) + kThreads / 32);
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
-    run_producer(p, &tmW, tmH.m, stage_base, c);
+    run_producer(p, q, &tmW, tmH.m, stage_base, c);
     __syncwarp();
   } else if (warp == 1) {
-    run_mma<kFmt>(p, stage_base, tmem_base, c);
+    run_mma<kFmt>(p, q, stage_base, tmem_base, c);
     __syncwarp();
   } else {
-    run_epilogue<T>(p, tmem_base, c, warp, lane);
+    run_epilogue<T>(p, q, tmem_base, c, warp, lane);
   }
 
   tc_fence_before_sync();
@@ -561,21 +652,11 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
   p.V = V;
   p.num_vtiles = (V + kBM - 1) / kBM;
   p.num_kblocks = (D + kBK - 1) / kBK;
-  // Panel of groups whose hidden states (a group holds up to ~2 * group_cols
-  // packed columns of D * 2 bytes) fit in ~48 MB of L2.
-  const long long group_bytes = 2 * fwd_group_cols(S) * static_cast<long long>(D) * 2;
-  long long pg = (48ll << 20) / (group_bytes > 0 ? group_bytes : 1);
-  if (pg < 1) pg = 1;
-  if (pg > B) pg = B;
-  p.panel_g = static_cast<int>(pg);
-  p.num_groups = ws.num_groups;
+  p.total_cols = ws.total_cols;
   p.pcol = ws.pcol;
   p.plen = ws.plen;
-  p.gstart = ws.gstart;
-  p.gcols = ws.gcols;
-  p.gword = ws.gword;
+  p.pnz = ws.pnz;
   p.prows = ws.prows;
-  p.gnz = ws.gnz;
   p.pvalid = ws.pvalid;
   p.prow = ws.prow;
   p.bias = bias;
@@ -597,8 +678,8 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
       attr_done[dev] = true;
     }
   }
-  // The number of units (vocab tiles x groups) is known on the device only;
-  // there are at most num_vtiles * B of them.
+  // The number of units (vocab tiles x groups) is chosen on the device; there
+  // are at most num_vtiles * B of them.
   const long long max_units = static_cast<long long>(p.num_vtiles) * B;
   const long long grid_ll = max_units < device_sm_count() ? max_units : device_sm_count();
   const unsigned grid = static_cast<unsigned>(grid_ll > 0 ? grid_ll : 1);

@@ -33,56 +33,43 @@ int device_sm_count();
 bool device_is_sm100();
 
 // ------------------------------------------------------------ forward workspace
-// [0,256)      header: u32 status, u32 number of position groups G, reserved
+// [0,256)      header: u32 status, u32 packed columns in total (T), reserved
 // extent       B x int32      last valid position + 1 of each row (0 = empty)
 // bits         B x S32 x u32  validity bit of every position, S32 = ceil(S/32)
-// Position packing for the tensor-core forward (written by pack_prepare):
-// the positions [0, round16(extent)) of consecutive batch rows are laid end to
-// end in a "packed column" stream, cut into groups of about fwd_group_cols(S)
-// columns (a group is a run of whole rows).
-// pcol         B x int32      packed column of row b's position 0 inside its group
+// Position packing for the tensor-core forward (written by pack_prepare): the
+// positions [0, round16(extent)) of all batch rows are laid end to end in one
+// stream of T "packed columns", row after row.
+// pcol         B x int32      packed column of row b's position 0
 // plen         B x int32      packed columns of row b: extent rounded up to 16
-// gstart       (B+1) x int32  first row of group g (gstart[G] = B)
-// gcols        (B+1) x int32  packed columns of group g
-// gword        (B+1) x int32  first bitmap word of group g (groups padded to 256)
-// prows        B x int32      the rows with packed columns, in order
-// gnz          (B+1) x int32  first entry of group g in prows (gnz[G] = count)
+// pnz          (B+1) x int32  rows with columns before row b (pnz[B] = count)
+// prows        B x int32      the rows with columns, in order
 // pvalid       Wmax x u32     validity bit of every packed column
 // prow         Wmax x u32     bit set at the first packed column of every row
-//              Wmax = B * round16(S) / 32 + 8 * B
+//              Wmax = ceil(B * round16(S) / 32) + 16 (the tail stays zero)
 struct FwdWorkspace {
   unsigned int* status;
-  unsigned int* num_groups;
+  unsigned int* total_cols;
   int* extent;
   uint32_t* bits;
   int S32;
   int* pcol;
   int* plen;
-  int* gstart;
-  int* gcols;
-  int* gword;
+  int* pnz;
   int* prows;
-  int* gnz;
   uint32_t* pvalid;
   uint32_t* prow;
   int64_t wmax;
 };
 
-// Packed columns per position group: at least 2048 and at least one whole
-// row (round16(S)), a multiple of the forward kernel's 256-column tile.
-inline int64_t fwd_group_cols(int64_t S) {
-  const int64_t row = (S + 15) / 16 * 16;
-  const int64_t g = row > 2048 ? row : 2048;
-  return (g + 255) / 256 * 256;
+inline int64_t fwd_packed_words(int64_t B, int64_t S) {
+  return (B * ((S + 15) / 16 * 16) + 31) / 32 + 16;
 }
-
-inline int64_t fwd_packed_words(int64_t B, int64_t S) { return B * ((S + 15) / 16 * 16) / 32 + 8 * B; }
 
 inline size_t fwd_workspace_bytes(int64_t B, int64_t S) {
   const int64_t S32 = (S + 31) / 32;
   const int64_t W = fwd_packed_words(B, S);
   return 256 + align256(static_cast<size_t>(B) * 4) + align256(static_cast<size_t>(B * S32) * 4) +
-         3 * align256(static_cast<size_t>(B) * 4) + 4 * align256(static_cast<size_t>(B + 1) * 4) +
+         3 * align256(static_cast<size_t>(B) * 4) + align256(static_cast<size_t>(B + 1) * 4) +
          2 * align256(static_cast<size_t>(W) * 4);
 }
 
@@ -90,7 +77,7 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
   FwdWorkspace w;
   char* base = static_cast<char*>(ws);
   w.status = reinterpret_cast<unsigned int*>(base);
-  w.num_groups = reinterpret_cast<unsigned int*>(base) + 1;
+  w.total_cols = reinterpret_cast<unsigned int*>(base) + 1;
   size_t off = 256;
   w.extent = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B) * 4);
@@ -101,15 +88,9 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
   off += align256(static_cast<size_t>(B) * 4);
   w.plen = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B) * 4);
-  w.gstart = reinterpret_cast<int*>(base + off);
-  off += align256(static_cast<size_t>(B + 1) * 4);
-  w.gcols = reinterpret_cast<int*>(base + off);
-  off += align256(static_cast<size_t>(B + 1) * 4);
-  w.gword = reinterpret_cast<int*>(base + off);
-  off += align256(static_cast<size_t>(B + 1) * 4);
   w.prows = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B) * 4);
-  w.gnz = reinterpret_cast<int*>(base + off);
+  w.pnz = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B + 1) * 4);
   w.wmax = fwd_packed_words(B, S);
   w.pvalid = reinterpret_cast<uint32_t*>(base + off);

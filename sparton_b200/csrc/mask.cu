@@ -9,10 +9,9 @@
 //
 // pack_prepare_kernel then lays the rows' positions end to end for the
 // tensor-core forward (workspace layout in internal.h): row b takes
-// round16(extent[b]) packed columns, consecutive rows follow each other, and
-// the stream is cut into groups of whole rows by the packed column at which
-// each row starts (group = start / group_cols). Per group it writes the
-// validity bit of every packed column and a bit at each row's first column.
+// round16(extent[b]) packed columns and consecutive rows follow each other. It
+// writes the validity bit of every packed column and a bit at each row's first
+// column, and the list of rows that have columns.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -92,111 +91,51 @@ __device__ __forceinline__ int block_scan_excl(int x, int* sh, int* total) {
   return excl;
 }
 
-// Group of the row whose packed columns start at global offset `start`.
-__device__ __forceinline__ int group_of_start(int start, int group_cols) { return start / group_cols; }
-
-// Last group g with gstart[g] <= b (groups are never empty).
-__device__ __forceinline__ int find_group(const int* gstart, int G, int b) {
-  int lo = 0, hi = G - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (gstart[mid] <= b) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
 __global__ void __launch_bounds__(kPackThreads)
-    pack_prepare_kernel(int B, int S32, int group_cols, const int* __restrict__ extent,
-                        const uint32_t* __restrict__ bits, int* pcol, int* plen, int* gstart,
-                        int* gcols, int* gword, int* prows, int* gnz, uint32_t* pvalid,
-                        uint32_t* prow, unsigned int* num_groups) {
+    pack_prepare_kernel(int B, int S32, const int* __restrict__ extent,
+                        const uint32_t* __restrict__ bits, int* pcol, int* plen, int* pnz,
+                        int* prows, uint32_t* pvalid, uint32_t* prow, unsigned int* total_cols) {
   __shared__ int sh[kPackThreads / 32 + 1];
   const int tid = threadIdx.x;
-  // 1. packed length of every row and its global start (exclusive prefix).
-  int carry = 0;
+  // 1. packed length and start of every row; the rows with columns, in order.
+  int carry = 0, carry_nz = 0;
   for (int base = 0; base < B; base += kPackThreads) {
     const int b = base + tid;
     const int len = b < B ? ((extent[b] + 15) & ~15) : 0;
-    int tot = 0;
+    int tot = 0, tot_nz = 0;
     const int ex = block_scan_excl(len, sh, &tot);
+    const int ex_nz = block_scan_excl(len > 0 ? 1 : 0, sh, &tot_nz);
     if (b < B) {
       plen[b] = len;
       pcol[b] = carry + ex;
+      pnz[b] = carry_nz + ex_nz;
+      if (len > 0) prows[carry_nz + ex_nz] = b;
     }
     carry += tot;
+    carry_nz += tot_nz;
   }
   const int total = carry;
-  __syncthreads();
-  // 2. group starts. A row is at most group_cols long, so consecutive rows'
-  // groups differ by at most 1 and no group is empty.
-  const int G = B > 0 ? group_of_start(pcol[B - 1], group_cols) + 1 : 0;
-  for (int b = tid; b < B; b += kPackThreads) {
-    const int g = group_of_start(pcol[b], group_cols);
-    const int gp = b > 0 ? group_of_start(pcol[b - 1], group_cols) : -1;
-    if (g != gp) gstart[g] = b;
-  }
   if (tid == 0) {
-    gstart[G] = B;
-    *num_groups = static_cast<unsigned int>(G);
+    pnz[B] = carry_nz;
+    *total_cols = static_cast<unsigned int>(total);
   }
-  __syncthreads();
-  // 3. columns of each group; its global start parked in gword for step 4.
-  for (int g = tid; g < G; g += kPackThreads) {
-    const int p0 = pcol[gstart[g]];
-    const int p1 = gstart[g + 1] < B ? pcol[gstart[g + 1]] : total;
-    gcols[g] = p1 - p0;
-    gword[g] = p0;
-  }
-  __syncthreads();
-  // 4. row start relative to its group.
-  for (int b = tid; b < B; b += kPackThreads) {
-    const int start = pcol[b];
-    pcol[b] = start - gword[group_of_start(start, group_cols)];
-  }
-  __syncthreads();
-  // 5. first bitmap word of each group (groups padded to whole 256-column tiles).
-  carry = 0;
-  for (int base = 0; base < G; base += kPackThreads) {
-    const int g = base + tid;
-    const int w = g < G ? (gcols[g] + 255) / 256 * 8 : 0;
-    int tot = 0;
-    const int ex = block_scan_excl(w, sh, &tot);
-    if (g < G) gword[g] = carry + ex;
-    carry += tot;
-  }
-  const int words = carry;
-  if (tid == 0) gword[G] = words;
+  // 2. clear the bitmaps (with the zero tail that the forward's reads may touch).
+  const int words = (total + 31) / 32 + 16;
   for (int i = tid; i < words; i += kPackThreads) {
     pvalid[i] = 0u;
     prow[i] = 0u;
   }
   __syncthreads();
-  // 6. the rows with columns, in order, and where each group's start in that list.
-  carry = 0;
-  for (int base = 0; base < B; base += kPackThreads) {
-    const int b = base + tid;
-    const int nz = (b < B && plen[b] > 0) ? 1 : 0;
-    int tot = 0;
-    const int ex = block_scan_excl(nz, sh, &tot);
-    if (nz) prows[carry + ex] = b;
-    if (b < B) {
-      const int g = find_group(gstart, G, b);
-      if (gstart[g] == b) gnz[g] = carry + ex;
-    }
-    carry += tot;
-  }
-  if (tid == 0) gnz[G] = carry;
-  // 7. bits of every row, 16 packed columns at a time (row starts and lengths
+  // 3. bits of every row, 16 packed columns at a time (row starts and lengths
   // are multiples of 16, so a word holds pieces of at most two rows).
   for (int b = tid; b < B; b += kPackThreads) {
     const int len = plen[b];
     if (len == 0) continue;
-    const int g = find_group(gstart, G, b);
-    const int c0 = pcol[b], w0 = gword[g];
+    const int c0 = pcol[b];
     const uint32_t* brow = bits + static_cast<size_t>(b) * S32;
     for (int x = 0; x < len; x += 16) {
       const int col = c0 + x;
-      const int word = w0 + (col >> 5), shift = col & 31;
+      const int word = col >> 5, shift = col & 31;
       const uint32_t v16 = (__ldg(brow + (x >> 5)) >> (x & 31)) & 0xFFFFu;
       if (v16 != 0u) atomicOr(pvalid + word, v16 << shift);
       if (x == 0) atomicOr(prow + word, 1u << shift);
@@ -210,9 +149,9 @@ int launch_typed(const void* mask, int B, int S, const FwdWorkspace& ws, cudaStr
                                                 ws.extent, ws.status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "mask_prepare_kernel launch");
-  pack_prepare_kernel<<<1, kPackThreads, 0, stream>>>(
-      B, ws.S32, static_cast<int>(fwd_group_cols(S)), ws.extent, ws.bits, ws.pcol, ws.plen,
-      ws.gstart, ws.gcols, ws.gword, ws.prows, ws.gnz, ws.pvalid, ws.prow, ws.num_groups);
+  pack_prepare_kernel<<<1, kPackThreads, 0, stream>>>(B, ws.S32, ws.extent, ws.bits, ws.pcol,
+                                                      ws.plen, ws.pnz, ws.prows, ws.pvalid,
+                                                      ws.prow, ws.total_cols);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "pack_prepare_kernel launch");
   return SPARTON_OK;

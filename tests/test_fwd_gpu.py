@@ -91,6 +91,28 @@ def test_all_rows_empty():
     assert (reps == 0).all() and (idx == 0).all()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rows_do_not_leak_into_each_other(dtype):
+    """The tensor-core forward lays the positions of consecutive rows end to end
+    and cuts that stream into tiles and work units. Rows here alternate between
+    hidden states of size ~1 and ~30 and have lengths of 16 mod 32 (a row or a
+    unit then ends in the middle of a 32-column chunk), so a position of the
+    next row counted into a row's max would show as a large error."""
+    B, S, D, V = 40, 200, 64, 300
+    gen = torch.Generator().manual_seed(11)
+    H = torch.randn(B, S, D, generator=gen)
+    H[1::2] *= 30.0
+    W = torch.randn(V, D, generator=gen) * (0.5 / D ** 0.5)
+    b = torch.randn(V, generator=gen) * 0.05
+    lengths = torch.tensor([16 + 32 * (i % 6) for i in range(B)])
+    lengths[5] = 0
+    lengths[17] = 0
+    mask = (torch.arange(S)[None, :] < lengths[:, None]).to(torch.int64)
+    H, W, b = H.to(dtype), W.to(dtype), b.to(dtype)
+    reps, idx = run_fwd(H, W, b, mask)
+    check_fwd(H, W, b, mask, reps, idx)
+
+
 @pytest.mark.parametrize("name", golden_names())
 def test_golden_fixtures_on_gpu(name):
     """Same inputs as the reference run that produced the fixture; fp64
