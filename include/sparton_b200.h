@@ -128,7 +128,8 @@ int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bia
 
 /* Size of the scratch array compiled into the library for
  * sparton_fwd_noalloc (1 MiB). It covers sparton_fwd_workspace_size(B,S,..)
- * <= 1 MiB, i.e. roughly B * (S/8 + 4) <= 1,040,000 (B=4096 rows at S=2048). */
+ * <= 1 MiB, i.e. roughly B * (3*S/8 + 24) bytes <= 1,048,576 (e.g. B=1024
+ * rows at S=2048, or B=4096 at S=512). */
 #define SPARTON_FWD_NOALLOC_SCRATCH_BYTES (1u << 20)
 
 /* sparton_fwd without a caller-provided workspace. No counterpart in the
