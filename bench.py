@@ -307,12 +307,25 @@ def main(argv=None) -> int:
                                             wsf.numel(), sh), "fwd")
         if k1 is not None:
             k1.record(stream)
+        if world == 1:
+            _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
+                                       Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs,
+                                       dH.data_ptr(), dW.data_ptr(), _lib.ptr(db),
+                                       _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
+                       "bwd")
+            return
+        # Sharded: partial dH, its all-reduce (NCCL's stream) overlapping dW / db,
+        # as SpartonHead's sharded backward does.
         _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
-                                   Wd.data_ptr(), dt, B, S, D, Vs, dH.data_ptr(), dW.data_ptr(),
+                                   Wd.data_ptr(), dt, B, S, D, Vs, dH.data_ptr(), None, None,
+                                   _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
+                   "bwd dH")
+        work = dist.all_reduce(dH, group=group, async_op=True)
+        _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
+                                   Wd.data_ptr(), dt, B, S, D, Vs, None, dW.data_ptr(),
                                    _lib.ptr(db), _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(),
-                                   wsb.numel(), sh), "bwd")
-        if world > 1:
-            dist.all_reduce(dH, group=group)
+                                   wsb.numel(), sh), "bwd dW")
+        work.wait()
 
     def barrier():
         if world > 1:

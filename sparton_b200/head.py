@@ -72,11 +72,19 @@ class _ShardedHead(torch.autograd.Function):
         reps, idx, hidden, weight = ctx.saved_tensors
         need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         need_b = ctx.has_bias and ctx.needs_input_grad[2]
-        d_hidden, d_weight, d_bias = ops.backward_impl(
-            grad_reps, reps, idx, hidden, weight, need_b, need_hidden=True, need_embed=need_w,
+        # The partial d_hidden first; its all-reduce (on the collective's own
+        # stream) then overlaps the d_weight / d_bias kernels.
+        d_hidden, _, _ = ops.backward_impl(
+            grad_reps, reps, idx, hidden, weight, False, need_hidden=True, need_embed=False,
             hidden_grad_dtype=ctx.reduce_dtype)
         # Every rank takes part in the all-reduce, whether or not it needs d_hidden.
-        dist.all_reduce(d_hidden, op=dist.ReduceOp.SUM, group=ctx.group)
+        work = dist.all_reduce(d_hidden, op=dist.ReduceOp.SUM, group=ctx.group, async_op=True)
+        d_weight = d_bias = None
+        if need_w or need_b:
+            _, d_weight, d_bias = ops.backward_impl(
+                grad_reps, reps, idx, hidden, weight, need_b, need_hidden=False,
+                need_embed=need_w)
+        work.wait()
         return (d_hidden if need_h else None, d_weight if need_w else None,
                 d_bias if need_b else None, None, None, None)
 
