@@ -175,6 +175,31 @@ int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx,
                 int d_hidden_dtype, int d_param_dtype,
                 void* workspace, size_t workspace_size, void* stream);
 
+/* ---------------------------------------------------------- regularisers */
+
+/* The sparsity regularisers that SPLADE training adds to its loss, on the
+ * head's output reps [B, V] (or one vocabulary shard of it), in one pass:
+ *   l1    = mean_b sum_v |reps[b, v]|       (training/train.py:80-82)
+ *   flops = mean_v (sum_b reps[b, v])^2     (training/train.py:85-87)
+ * Upstream computes them with separate torch reductions; there is no
+ * counterpart entry point upstream (these replace those two functions). */
+
+/* Bytes of workspace sparton_reg_fwd needs. */
+size_t sparton_reg_workspace_size(int64_t B, int64_t V);
+
+/* colsum[v] = sum_b reps[b, v] (fp32, [V], kept for the backward);
+ * totals[0] = sum |reps|, totals[1] = sum_v colsum[v]^2 (fp32, device).
+ * l1 = totals[0] / B and flops = totals[1] / V_total (after summing totals
+ * over the vocabulary shards). Deterministic. */
+int sparton_reg_fwd(const void* reps, int dtype, int64_t B, int64_t V, float* colsum,
+                    float* totals, void* workspace, size_t workspace_size, void* stream);
+
+/* grad[b, v] = coef[0] * sign(reps[b, v]) + coef[1] * colsum[v], in reps'
+ * dtype; coef (2 floats, device memory) = {dloss/dl1 / B,
+ * 2 * dloss/dflops / V_total}, so no value crosses to the host. */
+int sparton_reg_bwd(const void* reps, const float* colsum, const float* coef, int dtype,
+                    int64_t B, int64_t V, void* grad, void* stream);
+
 /* --------------------------------------------------------------- status */
 
 /* Copies the device status word of a workspace used by sparton_fwd /

@@ -156,6 +156,13 @@ int launch_fwd_f32(const float* hidden, const float* weight, const float* bias, 
                    int D, int V, float* reps, int32_t* idx, const FwdWorkspace& ws,
                    cudaStream_t stream);
 
+// Regularisers (reg.cu): workspace of block partials, fused forward / backward.
+size_t reg_workspace_bytes(int64_t V);
+int launch_reg_fwd(int dtype, const void* reps, int B, int V, float* colsum, float* totals,
+                   void* workspace, cudaStream_t stream);
+int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* coef, int B,
+                   int V, void* grad, cudaStream_t stream);
+
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,
                void* d_hidden, void* d_weight, void* d_bias, int d_hidden_dtype,

@@ -1,0 +1,210 @@
+// reg.cu — the sparsity regularisers of SPLADE training on the head's output
+// reps [B, V] (one vocabulary shard of it when the head is sharded), fused into
+// one pass over reps each way.
+//
+// Upstream (hhkbble/sparton training/train.py) computes them with separate
+// torch reductions:
+//   l1_regularization (:80-82)    = mean_b sum_v |reps[b, v]|
+//   flops_regularization (:85-87) = mean_v (sum_b reps[b, v])^2
+// Here reg_fwd_kernel reads reps once and produces the column sums
+// colsum[v] = sum_b reps[b, v] (kept for the backward) and, per block, the
+// partial sums of |reps| and of colsum^2; reg_total_kernel adds the block
+// partials in a fixed order (deterministic), giving totals = {sum |reps|,
+// sum_v colsum^2}. The caller divides by B and by the (whole) vocabulary size,
+// after summing the totals over shards. reg_bwd_kernel writes
+//   grad[b, v] = coef[0] * sign(reps[b, v]) + coef[1] * colsum[v]
+// with the coefficients read from device memory (upstream gradient / B and
+// 2 * upstream gradient / V), so the backward needs no host round trip.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "internal.h"
+
+namespace sparton {
+namespace {
+
+constexpr int kRegWarps = 8;  // rows are strided over the warps of a block
+constexpr int kTotalThreads = 1024;
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T* p);
+template <>
+__device__ __forceinline__ float load_f<float>(const float* p) {
+  return __ldg(p);
+}
+template <>
+__device__ __forceinline__ float load_f<__half>(const __half* p) {
+  return __half2float(__ldg(p));
+}
+template <>
+__device__ __forceinline__ float load_f<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(__ldg(p));
+}
+
+template <typename T>
+__device__ __forceinline__ T store_f(float x);
+template <>
+__device__ __forceinline__ float store_f<float>(float x) {
+  return x;
+}
+template <>
+__device__ __forceinline__ __half store_f<__half>(float x) {
+  return __float2half_rn(x);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 store_f<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// One block per 32 vocabulary columns (one per lane); warp w sums rows
+// b = w, w + 8, ... of its lane's column.
+template <typename T>
+__global__ void __launch_bounds__(kRegWarps * 32)
+    reg_fwd_kernel(const T* __restrict__ reps, int B, int V, float* __restrict__ colsum,
+                   float* __restrict__ partials) {
+  __shared__ float s_col[kRegWarps][32];
+  __shared__ float s_abs[kRegWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int v = blockIdx.x * 32 + lane;
+  float col = 0.f, ab = 0.f;
+  if (v < V) {
+    for (int b = warp; b < B; b += kRegWarps) {
+      const float x = load_f<T>(reps + static_cast<size_t>(b) * V + v);
+      col += x;
+      ab += fabsf(x);
+    }
+  }
+  s_col[warp][lane] = col;
+  s_abs[warp][lane] = ab;
+  __syncthreads();
+  if (warp == 0) {
+    float c = 0.f, a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRegWarps; ++w) {
+      c += s_col[w][lane];
+      a += s_abs[w][lane];
+    }
+    if (v < V) colsum[v] = c;
+    float sq = v < V ? c * c : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+    }
+    if (lane == 0) {
+      partials[2 * blockIdx.x] = a;
+      partials[2 * blockIdx.x + 1] = sq;
+    }
+  }
+}
+
+// One block: totals[k] = sum over blocks of partials[2*blk + k], in a fixed order.
+__global__ void __launch_bounds__(kTotalThreads)
+    reg_total_kernel(const float* __restrict__ partials, int nblocks, float* __restrict__ totals) {
+  __shared__ float s[2][kTotalThreads / 32];
+  float a = 0.f, q = 0.f;
+  for (int i = threadIdx.x; i < nblocks; i += kTotalThreads) {
+    a += partials[2 * i];
+    q += partials[2 * i + 1];
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+    q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s[0][warp] = a;
+    s[1][warp] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ta = 0.f, tq = 0.f;
+    for (int w = 0; w < kTotalThreads / 32; ++w) {
+      ta += s[0][w];
+      tq += s[1][w];
+    }
+    totals[0] = ta;
+    totals[1] = tq;
+  }
+}
+
+// Thread per column v (coalesced along a row); rows b = blockIdx.y, + gridDim.y, ...
+template <typename T>
+__global__ void __launch_bounds__(256)
+    reg_bwd_kernel(const T* __restrict__ reps, const float* __restrict__ colsum,
+                   const float* __restrict__ coef, int B, int V, T* __restrict__ grad) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= V) return;
+  const float c0 = __ldg(coef), c1 = __ldg(coef + 1);
+  const float cv = c1 * __ldg(colsum + v);
+  for (int b = blockIdx.y; b < B; b += gridDim.y) {
+    const size_t i = static_cast<size_t>(b) * V + v;
+    const float x = load_f<T>(reps + i);
+    const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+    grad[i] = store_f<T>(fmaf(c0, s, cv));
+  }
+}
+
+template <typename T>
+int launch_fwd_typed(const void* reps, int B, int V, float* colsum, float* totals,
+                     float* partials, cudaStream_t stream) {
+  const int nblocks = (V + 31) / 32;
+  reg_fwd_kernel<T><<<nblocks, kRegWarps * 32, 0, stream>>>(static_cast<const T*>(reps), B, V,
+                                                            colsum, partials);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "reg_fwd_kernel launch");
+  reg_total_kernel<<<1, kTotalThreads, 0, stream>>>(partials, nblocks, totals);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "reg_total_kernel launch");
+  return SPARTON_OK;
+}
+
+template <typename T>
+int launch_bwd_typed(const void* reps, const float* colsum, const float* coef, int B, int V,
+                     void* grad, cudaStream_t stream) {
+  const unsigned cols = static_cast<unsigned>((V + 255) / 256);
+  // Enough blocks for ~8 per SM, each covering a strided subset of the rows.
+  unsigned rows = static_cast<unsigned>((8ll * device_sm_count() + cols - 1) / cols);
+  if (rows > static_cast<unsigned>(B)) rows = static_cast<unsigned>(B);
+  if (rows < 1) rows = 1;
+  reg_bwd_kernel<T><<<dim3(cols, rows), 256, 0, stream>>>(
+      static_cast<const T*>(reps), colsum, coef, B, V, static_cast<T*>(grad));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "reg_bwd_kernel launch");
+  return SPARTON_OK;
+}
+
+}  // namespace
+
+size_t reg_workspace_bytes(int64_t V) { return align256(static_cast<size_t>((V + 31) / 32) * 8); }
+
+int launch_reg_fwd(int dtype, const void* reps, int B, int V, float* colsum, float* totals,
+                   void* workspace, cudaStream_t stream) {
+  float* partials = static_cast<float*>(workspace);
+  switch (dtype) {
+    case SPARTON_DTYPE_BF16:
+      return launch_fwd_typed<__nv_bfloat16>(reps, B, V, colsum, totals, partials, stream);
+    case SPARTON_DTYPE_F16:
+      return launch_fwd_typed<__half>(reps, B, V, colsum, totals, partials, stream);
+    case SPARTON_DTYPE_F32:
+      return launch_fwd_typed<float>(reps, B, V, colsum, totals, partials, stream);
+    default:
+      return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);
+  }
+}
+
+int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* coef, int B,
+                   int V, void* grad, cudaStream_t stream) {
+  switch (dtype) {
+    case SPARTON_DTYPE_BF16:
+      return launch_bwd_typed<__nv_bfloat16>(reps, colsum, coef, B, V, grad, stream);
+    case SPARTON_DTYPE_F16:
+      return launch_bwd_typed<__half>(reps, colsum, coef, B, V, grad, stream);
+    case SPARTON_DTYPE_F32:
+      return launch_bwd_typed<float>(reps, colsum, coef, B, V, grad, stream);
+    default:
+      return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);
+  }
+}
+
+}  // namespace sparton

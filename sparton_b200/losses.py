@@ -1,0 +1,151 @@
+"""Training losses that consume the head's output: hhkbble/sparton
+training/train.py:73-87, same names and arguments, plus a vocabulary-sharded
+form for representations that hold one vocabulary shard per rank (the output
+of ``SpartonHead(..., process_group=...)``):
+
+* ``info_nce_loss(query_reps, doc_reps, temperature=1.0, *, process_group=None)``
+  (train.py:73-77): ``scores = q @ d.T / temperature``, cross entropy against
+  the diagonal (in-batch negatives). Sharded, each rank scores its own
+  vocabulary shard and only the small ``[Bq, Bd]`` partial scores are
+  all-reduced (sum); the representations are never gathered. The backward is
+  local. Scores are accumulated in fp32 (upstream: in the reps' dtype).
+* ``l1_regularization(reps, *, process_group=None)`` (:80-82):
+  ``mean_b sum_v |reps|``.
+* ``flops_regularization(reps, *, process_group=None, vocab_size=None)``
+  (:85-87): ``mean_v (sum_b reps)^2``; ``vocab_size`` is the whole
+  vocabulary (when omitted with a process group, the shard widths are summed,
+  which reads one number back to the host).
+* ``regularizers(reps, ...) -> (l1, flops)``: both from one pass over reps
+  (``sparton_reg_fwd`` / ``sparton_reg_bwd``, csrc/reg.cu); the two functions
+  above call it. Sharded, the two totals are all-reduced.
+
+Loss values are fp32 scalars (upstream: the reps' dtype).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import _lib
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def reg_forward_impl(reps: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(colsum [V] fp32, totals [2] fp32 = {sum |reps|, sum_v colsum^2})."""
+    _require(reps.is_cuda, "the regularisers only support CUDA tensors")
+    _require(reps.dim() == 2, f"reps must be [B, V], got {tuple(reps.shape)}")
+    _require(reps.dtype in _lib.DTYPE, f"unsupported dtype {reps.dtype}")
+    lib = _lib.load()
+    reps = reps.contiguous()
+    B, V = reps.shape
+    dev = reps.device
+    colsum = torch.empty(V, dtype=torch.float32, device=dev)
+    totals = torch.empty(2, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(lib.sparton_reg_workspace_size(B, V), 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.sparton_reg_fwd(_lib.ptr(reps), _lib.DTYPE[reps.dtype], B, V, _lib.ptr(colsum),
+                                 _lib.ptr(totals), _lib.ptr(ws), ws.numel(), _lib.stream_handle(dev))
+    _lib.check(st, "sparton_reg_fwd")
+    return colsum, totals
+
+
+def reg_backward_impl(reps: torch.Tensor, colsum: torch.Tensor, coef: torch.Tensor) -> torch.Tensor:
+    """grad = coef[0] * sign(reps) + coef[1] * colsum[None, :], in reps' dtype."""
+    lib = _lib.load()
+    reps = reps.contiguous()
+    B, V = reps.shape
+    dev = reps.device
+    grad = torch.empty_like(reps)
+    coef = coef.to(device=dev, dtype=torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        st = lib.sparton_reg_bwd(_lib.ptr(reps), _lib.ptr(colsum), _lib.ptr(coef),
+                                 _lib.DTYPE[reps.dtype], B, V, _lib.ptr(grad),
+                                 _lib.stream_handle(dev))
+    _lib.check(st, "sparton_reg_bwd")
+    return grad
+
+
+def _vocab_total(width: int, device, group) -> int:
+    t = torch.tensor([width], dtype=torch.int64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return int(t.item())
+
+
+class _Regularizers(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, reps, group, vocab_size):
+        colsum, totals = reg_forward_impl(reps)
+        B, V = reps.shape
+        if group is not None:
+            dist.all_reduce(totals, op=dist.ReduceOp.SUM, group=group)
+            V = vocab_size if vocab_size is not None else _vocab_total(V, reps.device, group)
+        elif vocab_size is not None:
+            V = vocab_size
+        ctx.save_for_backward(reps, colsum)
+        ctx.B, ctx.V = B, V
+        return totals[0] / B, totals[1] / V
+
+    @staticmethod
+    def backward(ctx, g_l1, g_flops):
+        reps, colsum = ctx.saved_tensors
+        coef = torch.stack([g_l1.float() / ctx.B, 2.0 * g_flops.float() / ctx.V])
+        return reg_backward_impl(reps, colsum, coef), None, None
+
+
+def regularizers(reps: torch.Tensor, *, process_group=None,
+                 vocab_size: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(l1, flops) of ``reps`` [B, V] (a vocabulary shard with a process group)."""
+    return _Regularizers.apply(reps, process_group, vocab_size)
+
+
+def l1_regularization(reps: torch.Tensor, *, process_group=None) -> torch.Tensor:
+    """mean_b sum_v |reps[b, v]| (train.py:80-82)."""
+    return regularizers(reps, process_group=process_group)[0]
+
+
+def flops_regularization(reps: torch.Tensor, *, process_group=None,
+                         vocab_size: Optional[int] = None) -> torch.Tensor:
+    """mean_v (sum_b reps[b, v])^2 (train.py:85-87)."""
+    return regularizers(reps, process_group=process_group, vocab_size=vocab_size)[1]
+
+
+class _Scores(torch.autograd.Function):
+    """q @ d.T in fp32, summed over the vocabulary shards of a process group."""
+
+    @staticmethod
+    def forward(ctx, q, d, group):
+        s = torch.matmul(q.float(), d.float().t())
+        if group is not None:
+            dist.all_reduce(s, op=dist.ReduceOp.SUM, group=group)
+        ctx.save_for_backward(q, d)
+        return s
+
+    @staticmethod
+    def backward(ctx, gs):
+        q, d = ctx.saved_tensors
+        gq = (gs @ d.float()).to(q.dtype) if ctx.needs_input_grad[0] else None
+        gd = (gs.t() @ q.float()).to(d.dtype) if ctx.needs_input_grad[1] else None
+        return gq, gd, None
+
+
+def scores(query_reps: torch.Tensor, doc_reps: torch.Tensor, *, process_group=None) -> torch.Tensor:
+    """[Bq, Bd] dot products of query and document representations (fp32)."""
+    _require(query_reps.dim() == 2 and doc_reps.dim() == 2
+             and query_reps.shape[1] == doc_reps.shape[1],
+             "query_reps and doc_reps must be [Bq, V] and [Bd, V]")
+    return _Scores.apply(query_reps, doc_reps, process_group)
+
+
+def info_nce_loss(query_reps: torch.Tensor, doc_reps: torch.Tensor, temperature: float = 1.0,
+                  *, process_group=None) -> torch.Tensor:
+    """In-batch negatives contrastive loss (train.py:73-77)."""
+    s = scores(query_reps, doc_reps, process_group=process_group) / temperature
+    labels = torch.arange(s.size(0), device=s.device)
+    return F.cross_entropy(s, labels)
