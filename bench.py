@@ -265,6 +265,83 @@ def run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier, 
     return max_over_ranks(run(args.steps, True))
 
 
+def run_losses(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_ranks):
+    """The training losses that consume the head (sparton_b200.losses), timed at
+    the workload's reps shape [B, V_s] (queries and documents both B rows), L2
+    flushed before every iteration, CUDA events, max over ranks:
+    * reg_kernels: the fused regulariser kernels alone (csrc/reg.cu, C ABI);
+    * reg: l1 + flops regularisers, forward + backward through the autograd API;
+    * reg_torch: the same through upstream's torch formulation (train.py:80-87),
+      for comparison (single GPU only: it has no sharded form);
+    * info_nce: InfoNCE loss forward + backward, partial scores all-reduced
+      when sharded.
+    Algorithmic bytes of the fused regulariser pass: reps read twice (forward,
+    backward) and the gradient written once = 3 * B * V_s * 2 bytes."""
+    from sparton_b200 import _lib, losses
+
+    B = c["B"]
+    gen = torch.Generator().manual_seed(7)
+    q = (torch.rand(B, Vs, generator=gen) * 2).to(c["dtype"]).to(dev)
+    d = (torch.rand(B, Vs, generator=gen) * 2).to(c["dtype"]).to(dev)
+    V = c["V"]
+
+    def reg():
+        x = q.detach().requires_grad_(True)
+        l1, fl = losses.regularizers(x, process_group=group, vocab_size=V)
+        (l1 + fl).backward()
+
+    def reg_torch():
+        x = q.detach().requires_grad_(True)
+        l1 = torch.mean(torch.sum(torch.abs(x), dim=-1))
+        fl = torch.mean(torch.sum(x, dim=0) ** 2)
+        (l1 + fl).backward()
+
+    def nce():
+        a, b_ = q.detach().requires_grad_(True), d.detach().requires_grad_(True)
+        losses.info_nce_loss(a, b_, 1.0, process_group=group).backward()
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        barrier()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        barrier()
+        return max_over_ranks(sum(a.elapsed_time(e) for a, e in evs) / n)
+
+    # The two regulariser kernels alone, through the C ABI (no autograd around them).
+    lib = _lib.load()
+    colsum = torch.empty(Vs, dtype=torch.float32, device=dev)
+    pair = torch.empty(2, dtype=torch.float32, device=dev)
+    gpair = torch.ones(2, dtype=torch.float32, device=dev)
+    grad = torch.empty_like(q)
+    ws = torch.empty(lib.sparton_reg_workspace_size(B, Vs), dtype=torch.uint8, device=dev)
+    sh, dt = stream.cuda_stream, _lib.DTYPE[c["dtype"]]
+
+    def reg_kernels():
+        _lib.check(lib.sparton_reg_fwd(q.data_ptr(), dt, B, Vs, 1.0 / B, 1.0 / V, colsum.data_ptr(),
+                                       pair.data_ptr(), ws.data_ptr(), ws.numel(), sh), "reg_fwd")
+        _lib.check(lib.sparton_reg_bwd(q.data_ptr(), colsum.data_ptr(), gpair.data_ptr(),
+                                       gpair.data_ptr() + 4, 1.0 / B, 2.0 / V, dt, B, Vs,
+                                       grad.data_ptr(), sh), "reg_bwd")
+
+    out = {"shape": [B, Vs], "dtype": str(c["dtype"]).split(".")[-1]}
+    out["reg_kernels_ms"] = round(timed(reg_kernels), 4)
+    out["reg_fwd_bwd_ms"] = round(timed(reg), 4)
+    out["reg_algorithmic_bytes"] = 3 * B * Vs * 2
+    out["reg_kernels_gbs"] = round(out["reg_algorithmic_bytes"] / (out["reg_kernels_ms"] * 1e-3)
+                                   / 1e9, 1)
+    if world == 1:
+        out["reg_torch_fwd_bwd_ms"] = round(timed(reg_torch), 4)
+    out["info_nce_fwd_bwd_ms"] = round(timed(nce), 4)
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -272,9 +349,9 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU-baseline sample")
-    ap.add_argument("--legs", default="device,e2e,cpu",
-                    help="comma list of legs: device (value), e2e, cpu (baseline); "
-                         "profiling runs use --legs device")
+    ap.add_argument("--legs", default="device,e2e,cpu,losses",
+                    help="comma list of legs: device (value), e2e, cpu (baseline), losses "
+                         "(training losses on the head's output); profiling runs use --legs device")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -405,6 +482,11 @@ def main(argv=None) -> int:
                          max_over_ranks)
         h2d, d2h = e2e_bytes(H, mask, gs, B, Vs, c["dtype"])
 
+    losses_out = None
+    if "losses" in legs:
+        losses_out = run_losses(args, c, dev, group, world, Vs, flush, stream, barrier,
+                                max_over_ranks)
+
     # ------------------------------------------------------------ report
     peaks, peaks_src = load_peaks()
     fl = nominal_flops(c)
@@ -437,6 +519,7 @@ def main(argv=None) -> int:
             "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "path": "SpartonHead forward + autograd backward; pinned host inputs copied in and reps copied out every step, double-buffered on copy streams"},
+        "losses": losses_out,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }

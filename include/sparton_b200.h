@@ -188,17 +188,22 @@ int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx,
 size_t sparton_reg_workspace_size(int64_t B, int64_t V);
 
 /* colsum[v] = sum_b reps[b, v] (fp32, [V], kept for the backward);
- * totals[0] = sum |reps|, totals[1] = sum_v colsum[v]^2 (fp32, device).
- * l1 = totals[0] / B and flops = totals[1] / V_total (after summing totals
- * over the vocabulary shards). Deterministic. */
-int sparton_reg_fwd(const void* reps, int dtype, int64_t B, int64_t V, float* colsum,
-                    float* totals, void* workspace, size_t workspace_size, void* stream);
+ * out[0] = scale_l1 * sum |reps|, out[1] = scale_flops * sum_v colsum[v]^2
+ * (fp32, device). With scale_l1 = 1/B and scale_flops = 1/V_total these are
+ * the two losses; over vocabulary shards the outputs simply add up.
+ * Deterministic. */
+int sparton_reg_fwd(const void* reps, int dtype, int64_t B, int64_t V, float scale_l1,
+                    float scale_flops, float* colsum, float* out, void* workspace,
+                    size_t workspace_size, void* stream);
 
-/* grad[b, v] = coef[0] * sign(reps[b, v]) + coef[1] * colsum[v], in reps'
- * dtype; coef (2 floats, device memory) = {dloss/dl1 / B,
- * 2 * dloss/dflops / V_total}, so no value crosses to the host. */
-int sparton_reg_bwd(const void* reps, const float* colsum, const float* coef, int dtype,
-                    int64_t B, int64_t V, void* grad, void* stream);
+/* grad[b, v] = (*g_l1) * scale_l1 * sign(reps[b, v])
+ *            + (*g_flops) * scale_flops * colsum[v], in reps' dtype. g_l1 and
+ * g_flops point to one fp32 each in device memory (the upstream gradients of
+ * the two losses; NULL counts as 0); for the losses scale_l1 = 1/B and
+ * scale_flops = 2/V_total. No value crosses to the host. */
+int sparton_reg_bwd(const void* reps, const float* colsum, const float* g_l1,
+                    const float* g_flops, float scale_l1, float scale_flops, int dtype, int64_t B,
+                    int64_t V, void* grad, void* stream);
 
 /* --------------------------------------------------------------- status */
 

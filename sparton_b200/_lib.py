@@ -77,9 +77,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_bwd.restype = _i
     lib.sparton_reg_workspace_size.argtypes = [_i64, _i64]
     lib.sparton_reg_workspace_size.restype = _sz
-    lib.sparton_reg_fwd.argtypes = [_vp, _i, _i64, _i64, _vp, _vp, _vp, _sz, _vp]
+    _f = ctypes.c_float
+    lib.sparton_reg_fwd.argtypes = [_vp, _i, _i64, _i64, _f, _f, _vp, _vp, _vp, _sz, _vp]
     lib.sparton_reg_fwd.restype = _i
-    lib.sparton_reg_bwd.argtypes = [_vp, _vp, _vp, _i, _i64, _i64, _vp, _vp]
+    lib.sparton_reg_bwd.argtypes = [_vp, _vp, _vp, _vp, _f, _f, _i, _i64, _i64, _vp, _vp]
     lib.sparton_reg_bwd.restype = _i
     lib.sparton_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
     lib.sparton_read_device_status.restype = _i

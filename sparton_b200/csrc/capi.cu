@@ -241,33 +241,36 @@ size_t sparton_reg_workspace_size(int64_t B, int64_t V) {
   return reg_workspace_bytes(V);
 }
 
-int sparton_reg_fwd(const void* reps, int dtype, int64_t B, int64_t V, float* colsum,
-                    float* totals, void* workspace, size_t workspace_size, void* stream) {
+int sparton_reg_fwd(const void* reps, int dtype, int64_t B, int64_t V, float scale_l1,
+                    float scale_flops, float* colsum, float* out, void* workspace,
+                    size_t workspace_size, void* stream) {
   SPARTON_TRY(check_sizes(B, 0, 8, V));
   SPARTON_TRY(check_dtype(dtype));
   SPARTON_TRY(check_workspace(workspace, workspace_size, reg_workspace_bytes(V)));
-  if (totals == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "totals is NULL");
+  if (out == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "out is NULL");
   if (V > 0 && colsum == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "colsum is NULL");
   if (B * V > 0 && reps == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps is NULL");
   SPARTON_TRY(check_device());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (V == 0) {
-    const cudaError_t e = cudaMemsetAsync(totals, 0, 2 * sizeof(float), st);
+    const cudaError_t e = cudaMemsetAsync(out, 0, 2 * sizeof(float), st);
     return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "cudaMemsetAsync");
   }
-  return launch_reg_fwd(dtype, reps, static_cast<int>(B), static_cast<int>(V), colsum, totals,
-                        workspace, st);
+  return launch_reg_fwd(dtype, reps, static_cast<int>(B), static_cast<int>(V), scale_l1,
+                        scale_flops, colsum, out, workspace, st);
 }
 
-int sparton_reg_bwd(const void* reps, const float* colsum, const float* coef, int dtype,
-                    int64_t B, int64_t V, void* grad, void* stream) {
+int sparton_reg_bwd(const void* reps, const float* colsum, const float* g_l1,
+                    const float* g_flops, float scale_l1, float scale_flops, int dtype, int64_t B,
+                    int64_t V, void* grad, void* stream) {
   SPARTON_TRY(check_sizes(B, 0, 8, V));
   SPARTON_TRY(check_dtype(dtype));
   if (B * V == 0) return SPARTON_OK;
-  if (reps == nullptr || colsum == nullptr || coef == nullptr || grad == nullptr)
-    return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps / colsum / coef / grad is NULL");
+  if (reps == nullptr || colsum == nullptr || grad == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps / colsum / grad is NULL");
   SPARTON_TRY(check_device());
-  return launch_reg_bwd(dtype, reps, colsum, coef, static_cast<int>(B), static_cast<int>(V), grad,
+  return launch_reg_bwd(dtype, reps, colsum, g_l1, g_flops, scale_l1, scale_flops,
+                        static_cast<int>(B), static_cast<int>(V), grad,
                         static_cast<cudaStream_t>(stream));
 }
 

@@ -158,10 +158,11 @@ int launch_fwd_f32(const float* hidden, const float* weight, const float* bias, 
 
 // Regularisers (reg.cu): workspace of block partials, fused forward / backward.
 size_t reg_workspace_bytes(int64_t V);
-int launch_reg_fwd(int dtype, const void* reps, int B, int V, float* colsum, float* totals,
-                   void* workspace, cudaStream_t stream);
-int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* coef, int B,
-                   int V, void* grad, cudaStream_t stream);
+int launch_reg_fwd(int dtype, const void* reps, int B, int V, float scale_l1, float scale_flops,
+                   float* colsum, float* totals, void* workspace, cudaStream_t stream);
+int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* g_l1,
+                   const float* g_flops, float scale_l1, float scale_flops, int B, int V,
+                   void* grad, cudaStream_t stream);
 
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,

@@ -9,12 +9,13 @@
 // Here reg_fwd_kernel reads reps once and produces the column sums
 // colsum[v] = sum_b reps[b, v] (kept for the backward) and, per block, the
 // partial sums of |reps| and of colsum^2; reg_total_kernel adds the block
-// partials in a fixed order (deterministic), giving totals = {sum |reps|,
-// sum_v colsum^2}. The caller divides by B and by the (whole) vocabulary size,
-// after summing the totals over shards. reg_bwd_kernel writes
-//   grad[b, v] = coef[0] * sign(reps[b, v]) + coef[1] * colsum[v]
-// with the coefficients read from device memory (upstream gradient / B and
-// 2 * upstream gradient / V), so the backward needs no host round trip.
+// partials in a fixed order (deterministic) and scales them, giving
+// out = {scale_l1 * sum |reps|, scale_flops * sum_v colsum^2} (1/B and 1/V for
+// the losses; shards' outputs then simply add up). reg_bwd_kernel writes
+//   grad[b, v] = g_l1 * scale_l1 * sign(reps[b, v]) + g_flops * scale_flops * colsum[v]
+// with the upstream gradients g_l1, g_flops read from device memory (1/B and
+// 2/V as scales), so neither direction needs a host round trip or any
+// arithmetic outside the kernels.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(kRegWarps * 32)
   const int v = blockIdx.x * 32 + lane;
   float col = 0.f, ab = 0.f;
   if (v < V) {
+#pragma unroll 8
     for (int b = warp; b < B; b += kRegWarps) {
       const float x = load_f<T>(reps + static_cast<size_t>(b) * V + v);
       col += x;
@@ -98,9 +100,11 @@ __global__ void __launch_bounds__(kRegWarps * 32)
   }
 }
 
-// One block: totals[k] = sum over blocks of partials[2*blk + k], in a fixed order.
+// One block: out[k] = scale_k * sum over blocks of partials[2*blk + k], in a
+// fixed order.
 __global__ void __launch_bounds__(kTotalThreads)
-    reg_total_kernel(const float* __restrict__ partials, int nblocks, float* __restrict__ totals) {
+    reg_total_kernel(const float* __restrict__ partials, int nblocks, float scale_l1,
+                     float scale_flops, float* __restrict__ totals) {
   __shared__ float s[2][kTotalThreads / 32];
   float a = 0.f, q = 0.f;
   for (int i = threadIdx.x; i < nblocks; i += kTotalThreads) {
@@ -123,8 +127,8 @@ __global__ void __launch_bounds__(kTotalThreads)
       ta += s[0][w];
       tq += s[1][w];
     }
-    totals[0] = ta;
-    totals[1] = tq;
+    totals[0] = ta * scale_l1;
+    totals[1] = tq * scale_flops;
   }
 }
 
@@ -132,10 +136,12 @@ __global__ void __launch_bounds__(kTotalThreads)
 template <typename T>
 __global__ void __launch_bounds__(256)
     reg_bwd_kernel(const T* __restrict__ reps, const float* __restrict__ colsum,
-                   const float* __restrict__ coef, int B, int V, T* __restrict__ grad) {
+                   const float* __restrict__ g_l1, const float* __restrict__ g_flops,
+                   float scale_l1, float scale_flops, int B, int V, T* __restrict__ grad) {
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= V) return;
-  const float c0 = __ldg(coef), c1 = __ldg(coef + 1);
+  const float c0 = g_l1 != nullptr ? __ldg(g_l1) * scale_l1 : 0.f;
+  const float c1 = g_flops != nullptr ? __ldg(g_flops) * scale_flops : 0.f;
   const float cv = c1 * __ldg(colsum + v);
   for (int b = blockIdx.y; b < B; b += gridDim.y) {
     const size_t i = static_cast<size_t>(b) * V + v;
@@ -146,21 +152,23 @@ __global__ void __launch_bounds__(256)
 }
 
 template <typename T>
-int launch_fwd_typed(const void* reps, int B, int V, float* colsum, float* totals,
-                     float* partials, cudaStream_t stream) {
+int launch_fwd_typed(const void* reps, int B, int V, float scale_l1, float scale_flops,
+                     float* colsum, float* totals, float* partials, cudaStream_t stream) {
   const int nblocks = (V + 31) / 32;
   reg_fwd_kernel<T><<<nblocks, kRegWarps * 32, 0, stream>>>(static_cast<const T*>(reps), B, V,
                                                             colsum, partials);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reg_fwd_kernel launch");
-  reg_total_kernel<<<1, kTotalThreads, 0, stream>>>(partials, nblocks, totals);
+  reg_total_kernel<<<1, kTotalThreads, 0, stream>>>(partials, nblocks, scale_l1, scale_flops,
+                                                     totals);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reg_total_kernel launch");
   return SPARTON_OK;
 }
 
 template <typename T>
-int launch_bwd_typed(const void* reps, const float* colsum, const float* coef, int B, int V,
+int launch_bwd_typed(const void* reps, const float* colsum, const float* g_l1,
+                     const float* g_flops, float scale_l1, float scale_flops, int B, int V,
                      void* grad, cudaStream_t stream) {
   const unsigned cols = static_cast<unsigned>((V + 255) / 256);
   // Enough blocks for ~8 per SM, each covering a strided subset of the rows.
@@ -168,7 +176,8 @@ int launch_bwd_typed(const void* reps, const float* colsum, const float* coef, i
   if (rows > static_cast<unsigned>(B)) rows = static_cast<unsigned>(B);
   if (rows < 1) rows = 1;
   reg_bwd_kernel<T><<<dim3(cols, rows), 256, 0, stream>>>(
-      static_cast<const T*>(reps), colsum, coef, B, V, static_cast<T*>(grad));
+      static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, B, V,
+      static_cast<T*>(grad));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reg_bwd_kernel launch");
   return SPARTON_OK;
@@ -178,30 +187,37 @@ int launch_bwd_typed(const void* reps, const float* colsum, const float* coef, i
 
 size_t reg_workspace_bytes(int64_t V) { return align256(static_cast<size_t>((V + 31) / 32) * 8); }
 
-int launch_reg_fwd(int dtype, const void* reps, int B, int V, float* colsum, float* totals,
-                   void* workspace, cudaStream_t stream) {
+int launch_reg_fwd(int dtype, const void* reps, int B, int V, float scale_l1, float scale_flops,
+                   float* colsum, float* totals, void* workspace, cudaStream_t stream) {
   float* partials = static_cast<float*>(workspace);
   switch (dtype) {
     case SPARTON_DTYPE_BF16:
-      return launch_fwd_typed<__nv_bfloat16>(reps, B, V, colsum, totals, partials, stream);
+      return launch_fwd_typed<__nv_bfloat16>(reps, B, V, scale_l1, scale_flops, colsum, totals,
+                                             partials, stream);
     case SPARTON_DTYPE_F16:
-      return launch_fwd_typed<__half>(reps, B, V, colsum, totals, partials, stream);
+      return launch_fwd_typed<__half>(reps, B, V, scale_l1, scale_flops, colsum, totals, partials,
+                                      stream);
     case SPARTON_DTYPE_F32:
-      return launch_fwd_typed<float>(reps, B, V, colsum, totals, partials, stream);
+      return launch_fwd_typed<float>(reps, B, V, scale_l1, scale_flops, colsum, totals, partials,
+                                     stream);
     default:
       return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);
   }
 }
 
-int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* coef, int B,
-                   int V, void* grad, cudaStream_t stream) {
+int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float* g_l1,
+                   const float* g_flops, float scale_l1, float scale_flops, int B, int V,
+                   void* grad, cudaStream_t stream) {
   switch (dtype) {
     case SPARTON_DTYPE_BF16:
-      return launch_bwd_typed<__nv_bfloat16>(reps, colsum, coef, B, V, grad, stream);
+      return launch_bwd_typed<__nv_bfloat16>(reps, colsum, g_l1, g_flops, scale_l1, scale_flops, B,
+                                             V, grad, stream);
     case SPARTON_DTYPE_F16:
-      return launch_bwd_typed<__half>(reps, colsum, coef, B, V, grad, stream);
+      return launch_bwd_typed<__half>(reps, colsum, g_l1, g_flops, scale_l1, scale_flops, B, V,
+                                      grad, stream);
     case SPARTON_DTYPE_F32:
-      return launch_bwd_typed<float>(reps, colsum, coef, B, V, grad, stream);
+      return launch_bwd_typed<float>(reps, colsum, g_l1, g_flops, scale_l1, scale_flops, B, V,
+                                     grad, stream);
     default:
       return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);
   }

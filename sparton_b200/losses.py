@@ -37,8 +37,10 @@ def _require(cond: bool, msg: str) -> None:
         raise ValueError(msg)
 
 
-def reg_forward_impl(reps: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """(colsum [V] fp32, totals [2] fp32 = {sum |reps|, sum_v colsum^2})."""
+def reg_forward_impl(reps: torch.Tensor, scale_l1: float,
+                     scale_flops: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(colsum [V] fp32, out [2] fp32 = {scale_l1 * sum |reps|,
+    scale_flops * sum_v colsum^2})."""
     _require(reps.is_cuda, "the regularisers only support CUDA tensors")
     _require(reps.dim() == 2, f"reps must be [B, V], got {tuple(reps.shape)}")
     _require(reps.dtype in _lib.DTYPE, f"unsupported dtype {reps.dtype}")
@@ -47,27 +49,30 @@ def reg_forward_impl(reps: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     B, V = reps.shape
     dev = reps.device
     colsum = torch.empty(V, dtype=torch.float32, device=dev)
-    totals = torch.empty(2, dtype=torch.float32, device=dev)
+    out = torch.empty(2, dtype=torch.float32, device=dev)
     ws = torch.empty(max(lib.sparton_reg_workspace_size(B, V), 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        st = lib.sparton_reg_fwd(_lib.ptr(reps), _lib.DTYPE[reps.dtype], B, V, _lib.ptr(colsum),
-                                 _lib.ptr(totals), _lib.ptr(ws), ws.numel(), _lib.stream_handle(dev))
+        st = lib.sparton_reg_fwd(_lib.ptr(reps), _lib.DTYPE[reps.dtype], B, V, scale_l1,
+                                 scale_flops, _lib.ptr(colsum), _lib.ptr(out), _lib.ptr(ws),
+                                 ws.numel(), _lib.stream_handle(dev))
     _lib.check(st, "sparton_reg_fwd")
-    return colsum, totals
+    return colsum, out
 
 
-def reg_backward_impl(reps: torch.Tensor, colsum: torch.Tensor, coef: torch.Tensor) -> torch.Tensor:
-    """grad = coef[0] * sign(reps) + coef[1] * colsum[None, :], in reps' dtype."""
+def reg_backward_impl(reps: torch.Tensor, colsum: torch.Tensor, g: torch.Tensor,
+                      scale_l1: float, scale_flops: float) -> torch.Tensor:
+    """grad = g[0] * scale_l1 * sign(reps) + g[1] * scale_flops * colsum[None, :],
+    in reps' dtype (g: the upstream gradients of (l1, flops), fp32 on the device)."""
     lib = _lib.load()
     reps = reps.contiguous()
     B, V = reps.shape
     dev = reps.device
     grad = torch.empty_like(reps)
-    coef = coef.to(device=dev, dtype=torch.float32).contiguous()
+    g = g.to(device=dev, dtype=torch.float32).contiguous()
     with torch.cuda.device(dev):
-        st = lib.sparton_reg_bwd(_lib.ptr(reps), _lib.ptr(colsum), _lib.ptr(coef),
-                                 _lib.DTYPE[reps.dtype], B, V, _lib.ptr(grad),
-                                 _lib.stream_handle(dev))
+        st = lib.sparton_reg_bwd(_lib.ptr(reps), _lib.ptr(colsum), _lib.ptr(g), _lib.ptr(g) + 4,
+                                 scale_l1, scale_flops, _lib.DTYPE[reps.dtype], B, V,
+                                 _lib.ptr(grad), _lib.stream_handle(dev))
     _lib.check(st, "sparton_reg_bwd")
     return grad
 
@@ -81,28 +86,31 @@ def _vocab_total(width: int, device, group) -> int:
 class _Regularizers(torch.autograd.Function):
     @staticmethod
     def forward(ctx, reps, group, vocab_size):
-        colsum, totals = reg_forward_impl(reps)
         B, V = reps.shape
         if group is not None:
-            dist.all_reduce(totals, op=dist.ReduceOp.SUM, group=group)
             V = vocab_size if vocab_size is not None else _vocab_total(V, reps.device, group)
         elif vocab_size is not None:
             V = vocab_size
+        # The kernel scales its sums (1/B, 1/V), so a shard's two values add up
+        # over the group to the losses.
+        colsum, out = reg_forward_impl(reps, 1.0 / B, 1.0 / V)
+        if group is not None:
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
         ctx.save_for_backward(reps, colsum)
         ctx.B, ctx.V = B, V
-        return totals[0] / B, totals[1] / V
+        return out
 
     @staticmethod
-    def backward(ctx, g_l1, g_flops):
+    def backward(ctx, g):
         reps, colsum = ctx.saved_tensors
-        coef = torch.stack([g_l1.float() / ctx.B, 2.0 * g_flops.float() / ctx.V])
-        return reg_backward_impl(reps, colsum, coef), None, None
+        return reg_backward_impl(reps, colsum, g, 1.0 / ctx.B, 2.0 / ctx.V), None, None
 
 
 def regularizers(reps: torch.Tensor, *, process_group=None,
                  vocab_size: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """(l1, flops) of ``reps`` [B, V] (a vocabulary shard with a process group)."""
-    return _Regularizers.apply(reps, process_group, vocab_size)
+    l1, flops = _Regularizers.apply(reps, process_group, vocab_size).unbind(0)
+    return l1, flops
 
 
 def l1_regularization(reps: torch.Tensor, *, process_group=None) -> torch.Tensor:
@@ -121,7 +129,10 @@ class _Scores(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, d, group):
-        s = torch.matmul(q.float(), d.float().t())
+        if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and d.dtype == q.dtype:
+            s = torch.mm(q, d.t(), out_dtype=torch.float32)  # 16-bit inputs, fp32 sums
+        else:
+            s = torch.matmul(q.float(), d.float().t())
         if group is not None:
             dist.all_reduce(s, op=dist.ReduceOp.SUM, group=group)
         ctx.save_for_backward(q, d)

@@ -29,15 +29,16 @@ def _inputs():
     return q, d
 
 
-def _cpu_reg_forward(reps):
+def _cpu_reg_forward(reps, scale_l1, scale_flops):
     x = reps.detach().double()
     col = x.sum(0)
-    return col.float(), torch.stack([x.abs().sum(), (col ** 2).sum()]).float()
+    return col.float(), torch.stack([x.abs().sum() * scale_l1, (col ** 2).sum() * scale_flops]).float()
 
 
-def _cpu_reg_backward(reps, colsum, coef):
-    return (coef[0].double() * torch.sign(reps.detach().double())
-            + coef[1].double() * colsum.double()[None, :]).to(reps.dtype)
+def _cpu_reg_backward(reps, colsum, g, scale_l1, scale_flops):
+    g = g.double()
+    return (g[0] * scale_l1 * torch.sign(reps.detach().double())
+            + g[1] * scale_flops * colsum.double()[None, :]).to(reps.dtype)
 
 
 def _worker(rank, world, port, out_dir):
