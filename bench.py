@@ -1,13 +1,16 @@
 """Benchmark of the B200-native SPLADE head: fused forward + backward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload config2|config3|config4|config5]
     (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
 
-Workload (the configuration its metric is quoted on):
-B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden ~ N(0,1),
-W ~ N(0,0.02), bias ~ N(0,0.02), right-padded mask with lengths U[32,256],
-upstream grad g ~ N(0,1); seeded synthetic data standing in for SPLADE
-batches. With N GPUs the decoder is vocabulary-sharded over the ranks (the same
+Default workload (the configuration its metric is
+quoted on): B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden
+~ N(0,1), W ~ N(0,0.02), bias ~ N(0,0.02), right-padded mask with lengths
+U[32,256], upstream grad g ~ N(0,1); seeded synthetic data standing in for
+SPLADE batches. ``--workload`` selects the other BASELINE configurations
+(WORKLOADS below: config 3 V=250002, config 4 fp16 B=512 S=512, config 5
+D=4096 V=128256 without bias), same distributions as BASELINE.json states. With N GPUs the decoder is vocabulary-sharded over the ranks (the same
 total workload: strong scaling) and the partial d_hidden is all-reduced (fp32,
 NCCL).
 
@@ -46,8 +49,24 @@ if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
 METRIC = "fused head fwd+bwd TFLOP/s (4·B·S·D·V) & tokens/s at 1/2/4/8 B200; % of bf16 peak"
-CFG = dict(name="config 2 (BERT-base SPLADE head)", B=128, S=256, D=768, V=30522,
-           dtype=torch.bfloat16, lengths=(32, 256), bias=True, w_std=0.02)
+# BASELINE.json configs[1..4] ("config 2" .. "config 5"). Config 2 is the one the
+# metric is quoted on and the default; the others are selected with --workload.
+WORKLOADS = {
+    "config2": dict(name="config 2 (BERT-base SPLADE head)", B=128, S=256, D=768, V=30522,
+                    dtype=torch.bfloat16, lengths=(32, 256), bias=True, w_std=0.02,
+                    full_frac=0.0, cpu_rows=8),
+    "config3": dict(name="config 3 (XLM-R-base large-vocab head)", B=32, S=256, D=768, V=250002,
+                    dtype=torch.bfloat16, lengths=(32, 256), bias=True, w_std=0.02,
+                    full_frac=0.0, cpu_rows=2),
+    "config4": dict(name="config 4 (long-sequence head)", B=512, S=512, D=768, V=30522,
+                    dtype=torch.float16, lengths=(64, 512), bias=True, w_std=0.02,
+                    full_frac=0.1, cpu_rows=4),
+    "config5": dict(name="config 5 (decoder-LLM-size head)", B=64, S=1024, D=4096, V=128256,
+                    dtype=torch.bfloat16, lengths=(256, 1024), bias=False, w_std=0.01,
+                    full_frac=0.0, cpu_rows=1),
+}
+CFG = WORKLOADS["config2"]
+DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
 L2_FLUSH_BYTES = 256 << 20
 
@@ -69,6 +88,9 @@ def make_inputs(c, seed=0):
     b = (torch.randn(V, generator=gen) * 0.02).to(c["dtype"]) if c["bias"] else None
     lo, hi = c["lengths"]
     L = torch.randint(lo, hi + 1, (B,), generator=gen)
+    if c.get("full_frac", 0.0) > 0:  # config 4: a fraction of the rows at full length
+        full = torch.rand(B, generator=gen) < c["full_frac"]
+        L = torch.where(full, torch.full_like(L, S), L)
     mask = (torch.arange(S)[None, :] < L[:, None]).to(torch.int64)
     g = torch.randn(B, V, generator=gen).to(c["dtype"])
     return H, W, b, mask, g, L
@@ -84,9 +106,17 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per forward launch from the committed ncu summary, if any."""
-    path = os.path.join(REPO, "profiles", "fwd_tc_config2_traffic.txt")
+def workload_desc(c) -> str:
+    lo, hi = c["lengths"]
+    full = f", {int(c['full_frac'] * 100)}% of rows full length" if c.get("full_frac") else ""
+    return (f"{c['name']}: B={c['B']} S={c['S']} D={c['D']} V={c['V']} {DTYPE_NAME[c['dtype']]}, "
+            f"lengths U[{lo},{hi}]{full}, {'bias' if c['bias'] else 'no bias'}")
+
+
+def profile_traffic(workload: str):
+    """DRAM bytes per forward launch from the committed ncu summary of this
+    workload, if any."""
+    path = os.path.join(REPO, "profiles", f"fwd_tc_{workload}_traffic.txt")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -157,7 +187,7 @@ def cpu_baseline(c, sample_rows: int, steps: int, warmup: int) -> dict:
 
     _, _, _, _, _, L = make_inputs(dict(c, B=sample_rows), seed=1)
     r = time_fwd_bwd(sample_rows, c["S"], c["D"], c["V"], L.tolist(), use_bias=c["bias"],
-                     steps=steps, warmup=warmup)
+                     steps=steps, warmup=warmup, w_std=c["w_std"])
     flops = 4.0 * sample_rows * c["S"] * c["D"] * c["V"]
     return {"value": flops / r["seconds_per_step"] / 1e12, "unit": "TFLOP/s",
             "cores": r["threads"], "kind": "port",
@@ -169,8 +199,8 @@ def cpu_baseline(c, sample_rows: int, steps: int, warmup: int) -> dict:
 def run_reference_arm(args, rank: int) -> int:
     if rank != 0:
         return 0
-    c = CFG
-    rows = 8
+    c = WORKLOADS[args.workload]
+    rows = args.cpu_rows or c["cpu_rows"]
     res = cpu_baseline(c, rows, steps=args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "TFLOP/s",
@@ -178,7 +208,7 @@ def run_reference_arm(args, rank: int) -> int:
         "ms_per_step": res["seconds_per_step"] * 1e3 * c["B"] / rows,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "config 2: B=128 S=256 D=768 V=30522, lengths U[32,256]",
+        "config": {"workload": workload_desc(c),
                    "B": c["B"], "S": c["S"], "D": c["D"], "V": c["V"],
                    "per_step_sample_rows": rows, "device": "host CPU"},
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -348,7 +378,10 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU-baseline sample")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
+                    help="BASELINE configuration (default config2, the one the metric is quoted on)")
+    ap.add_argument("--cpu-rows", type=int, default=None,
+                    help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--legs", default="device,e2e,cpu,losses",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
                          "(training losses on the head's output); profiling runs use --legs device")
@@ -381,7 +414,7 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
 
-    c = CFG
+    c = WORKLOADS[args.workload]
     B, S, D, V = c["B"], c["S"], c["D"], c["V"]
     H, W, b, mask, g, L = make_inputs(c)
     T = int(L.sum())
@@ -494,13 +527,14 @@ def main(argv=None) -> int:
     alg_fwd = 2.0 * D * Vs * T  # this rank's forward launch
     achieved = alg_fwd / (kern_ms * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    traffic = profile_traffic() if world == 1 else None
+    traffic = profile_traffic(args.workload) if world == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded; BASELINE config 2 distributions)",
-        "config": {"workload": "config 2: B=128 S=256 D=768 V=30522 bf16, lengths U[32,256], bias",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": DTYPE_NAME[c["dtype"]],
+        "data": f"synthetic (seeded; BASELINE {c['name'].split(' (')[0]} distributions)",
+        "config": {"workload": workload_desc(c),
                    "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
                    "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
                    "l2": "flushed (256 MiB write) before every timed step"},
@@ -525,7 +559,7 @@ def main(argv=None) -> int:
     }
     if rank == 0 and world == 1 and "cpu" in legs:
         try:
-            res = cpu_baseline(c, args.cpu_rows, steps=3, warmup=1)
+            res = cpu_baseline(c, args.cpu_rows or c["cpu_rows"], steps=3, warmup=1)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
         except Exception as e:  # pragma: no cover
             line["cpu_baseline"] = {"error": repr(e)}

@@ -24,14 +24,14 @@ def torch_head(hidden: torch.Tensor, weight: torch.Tensor, bias, mask: torch.Ten
 
 def time_fwd_bwd(B: int, S: int, D: int, V: int, lengths, use_bias: bool = True, steps: int = 3,
                  warmup: int = 1, threads: int | None = None, seed: int = 0,
-                 dtype: torch.dtype = torch.float32) -> dict:
+                 dtype: torch.dtype = torch.float32, w_std: float = 0.02) -> dict:
     """Times fwd+bwd of the torch head on the host (fp32 by default, every
     host thread). Returns seconds per step and the thread count used."""
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     gen = torch.Generator().manual_seed(seed)
     H = torch.randn(B, S, D, generator=gen, dtype=dtype).requires_grad_(True)
-    W = (torch.randn(V, D, generator=gen) * 0.02).to(dtype).requires_grad_(True)
+    W = (torch.randn(V, D, generator=gen) * w_std).to(dtype).requires_grad_(True)
     b = (torch.randn(V, generator=gen) * 0.02).to(dtype).requires_grad_(True) if use_bias else None
     mask = torch.zeros(B, S, dtype=torch.int64)
     for i, L in enumerate(lengths):

@@ -22,12 +22,16 @@
 //   K4 gather_kernel<1>  one warp per vocab id: dW[v,:] = sum over b of
 //                        g' * H[b*S + idx[b,v], :] (neighbouring vocab ids share
 //                        H[b] rows in L1); db[v] is the sum of the same g'.
+//                        K3 and K4 cut D into column slices, slice-major, when
+//                        the gathered matrix (W for K3, H for K4) exceeds the
+//                        L2 budget, so the slice being gathered stays in L2.
 //      db_kernel         db alone, when dW is not requested.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -72,30 +76,6 @@ __device__ __forceinline__ __half cvt_out<__half>(float x) {
   return __float2half_rn(x);
 }
 
-template <typename O>
-__device__ __forceinline__ void store8(O* p, const float (&x)[8]);
-template <>
-__device__ __forceinline__ void store8<float>(float* p, const float (&x)[8]) {
-  reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
-  reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
-}
-template <>
-__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&x)[8]) {
-  uint4 u;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = u;
-}
-template <>
-__device__ __forceinline__ void store8<__half>(__half* p, const float (&x)[8]) {
-  uint4 u;
-  __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = u;
-}
-
 // acc[i], acc[i+1] += c * f.x, c * f.y as one paired FMA (fma.rn.f32x2 on
 // sm_100): the same per-element rounding as two fmaf, half the instructions.
 __device__ __forceinline__ void fma2(float c, float2 f, float (&acc)[8], int i) {
@@ -107,40 +87,21 @@ __device__ __forceinline__ void fma2(float c, float2 f, float (&acc)[8], int i) 
 // Eight consecutive elements of a row (16-bit types: one 16-byte load; fp32:
 // two) and their FMA into eight fp32 accumulators.
 template <typename T>
-struct Row8;
-template <>
-struct Row8<__nv_bfloat16> {
+struct Row8 {  // 16-bit element types
   uint4 r;
-  __device__ __forceinline__ void load(const __nv_bfloat16* p) {
-    r = __ldg(reinterpret_cast<const uint4*>(p));
-  }
-  __device__ __forceinline__ void load_smem(const __nv_bfloat16* p) {
-    r = *reinterpret_cast<const uint4*>(p);
-  }
+  __device__ __forceinline__ void load(const T* p) { r = __ldg(reinterpret_cast<const uint4*>(p)); }
   __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
   __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
-    // bf16 -> fp32 is a 16-bit shift.
     const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      fma2(c, make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u)), acc,
-           2 * i);
-  }
-};
-template <>
-struct Row8<__half> {
-  uint4 r;
-  __device__ __forceinline__ void load(const __half* p) {
-    r = __ldg(reinterpret_cast<const uint4*>(p));
-  }
-  __device__ __forceinline__ void load_smem(const __half* p) {
-    r = *reinterpret_cast<const uint4*>(p);
-  }
-  __device__ __forceinline__ void zero() { r = make_uint4(0u, 0u, 0u, 0u); }
-  __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
-    const __half2* h = reinterpret_cast<const __half2*>(&r);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) fma2(c, __half22float2(h[i]), acc, 2 * i);
+    for (int i = 0; i < 4; ++i) {
+      float2 f;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value)  // bf16 -> fp32: a 16-bit shift
+        f = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+      else
+        f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      fma2(c, f, acc, 2 * i);
+    }
   }
 };
 template <>
@@ -149,10 +110,6 @@ struct Row8<float> {
   __device__ __forceinline__ void load(const float* p) {
     a = __ldg(reinterpret_cast<const float4*>(p));
     b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  }
-  __device__ __forceinline__ void load_smem(const float* p) {
-    a = *reinterpret_cast<const float4*>(p);
-    b = *(reinterpret_cast<const float4*>(p) + 1);
   }
   __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
   __device__ __forceinline__ void fma_into(float c, float (&acc)[8]) const {
@@ -163,6 +120,27 @@ struct Row8<float> {
   }
 };
 
+// Eight fp32 values stored as eight elements of O (one 16-byte store for 16-bit O).
+template <typename O>
+__device__ __forceinline__ void store8(O* p, const float (&x)[8]) {
+  if constexpr (std::is_same<O, float>::value) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<O, __nv_bfloat16>::value) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        memcpy(&w[i], &h, 4);
+      } else {
+        const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        memcpy(&w[i], &h, 4);
+      }
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
 
 // ------------------------------------------------------------------ K2: sort
 // One block per batch row, `nw` warps. Warp w owns the contiguous vocab range
@@ -311,28 +289,42 @@ __global__ void __launch_bounds__(256)
 }
 
 // ----------------------------------------------------------- K3/K4: dH, dW
-// out[r,:] = sum over the entry list of row r of coef * src[row, :], one warp
-// per output row, 8 warps per CTA:
+// out[r, :] = sum over the entry list of row r of coef * src[row, :], 8 warps
+// per CTA:
 //   kMode 0 (dH): r = b*S + s, entries = bucket (b, s) of the CSR
 //                 (src row = v, coef = g'), src = W;
 //   kMode 1 (dW): r = v, entries = its B vocab-major entries (src row =
 //                 b*S + idx[b,v], coef = g'), src = H; out_sum[r] = db[v].
-// A pass covers NC*256 columns (lane l owns columns d0 + c*256 + 8l .. +7).
 // Entries are fetched 32 at a time with one coalesced load and broadcast by
-// shuffle; for each group of 4 entries all row loads of the pass are issued
-// before the FMAs (4*NC 16-byte loads per lane in flight). For dW, neighbouring
-// vocab ids walk the batch rows in step, so the rows of H[b] they share are
-// served from L1.
+// shuffle, and the loads of several entries are issued before their FMAs.
+//
+// Full rows (one warp per output row): lane l owns columns d0 + c*256 + 8l ..
+// +7 of NC*256-column passes; 4 entries, NC 16-byte loads each, in flight per
+// lane. For dW, neighbouring vocab ids walk the batch rows in step, so the rows
+// of H[b] they share are served from L1.
+//
+// Column slices, for a gathered working set larger than the L2 budget (all of
+// W for dH, whose rows are gathered in random order; for dW the rows of the
+// ~16 batch rows that the warps in flight walk together): D is cut into
+// slices of 256, 128 or 64 columns and the work items (slice, row) are
+// slice-major, so the warps in flight all read one slice of src, which stays
+// in L2. A warp takes one (slice, row) item split into G = 256 / slice lane
+// groups; each lane loads 8 columns (16 bytes) and group g takes the entries
+// j with j % G == g, so every load stays 16 bytes wide; the G partial sums are
+// added in a fixed butterfly order at the end (deterministic). The next entry
+// batch is prefetched while the current one is gathered.
 constexpr int kGWarps = 8;
 constexpr int kGUnroll = 4;
+// Bytes of gathered data that are expected to stay resident in the 126 MB L2
+// next to the other traffic of the kernel, and the batch rows that the dW
+// warps in flight span.
+constexpr long long kGatherL2Budget = 48ll << 20;
+constexpr int kDwRowsInFlight = 16;
 
-template <typename T, typename O, int NC, int kMode>
-__device__ __forceinline__ void gather_row(const T* __restrict__ src, int B, int S, int D, int V,
-                                           const int* __restrict__ offs,
-                                           const int* __restrict__ ent_row,
-                                           const float* __restrict__ ent_coef, int q,
-                                           O* __restrict__ out, O* __restrict__ out_sum, int lane) {
-  int r, e0, e1;
+// Row bounds of an output row: r and its entries [e0, e1).
+template <int kMode>
+__device__ __forceinline__ void entry_range(int q, int B, int S, int V, const int* __restrict__ offs,
+                                            int& r, int& e0, int& e1) {
   if (kMode == 0) {
     const int s = q / B, b = q - (q / B) * B;
     r = b * S + s;
@@ -344,6 +336,17 @@ __device__ __forceinline__ void gather_row(const T* __restrict__ src, int B, int
     e0 = r * B;
     e1 = e0 + B;
   }
+}
+
+template <typename T, typename O, int NC, int kMode>
+__device__ __forceinline__ void gather_row_full(const T* __restrict__ src, int B, int S, int D,
+                                                int V, const int* __restrict__ offs,
+                                                const int* __restrict__ ent_row,
+                                                const float* __restrict__ ent_coef, int q,
+                                                O* __restrict__ out, O* __restrict__ out_sum,
+                                                int lane) {
+  int r, e0, e1;
+  entry_range<kMode>(q, B, S, V, offs, r, e0, e1);
   O* orow = out + static_cast<size_t>(r) * D;
   float csum = 0.f;
   for (int d0 = 0; d0 < D; d0 += NC * 256) {
@@ -399,33 +402,128 @@ __device__ __forceinline__ void gather_row(const T* __restrict__ src, int B, int
   }
 }
 
+// Columns [d_lo, d_lo + width) of one output row, width <= 256 / G.
+template <typename T, typename O, int G, int U, int kMode>
+__device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int B, int S, int D,
+                                                 int V, const int* __restrict__ offs,
+                                                 const int* __restrict__ ent_row,
+                                                 const float* __restrict__ ent_coef, int q,
+                                                 int d_lo, int width, O* __restrict__ out,
+                                                 O* __restrict__ out_sum, int lane) {
+  static_assert(G == 1 || G == 2 || G == 4, "lane groups");
+  static_assert(U * G <= 32 && 32 % (U * G) == 0, "entries per round must divide 32");
+  constexpr int kLanes = 32 / G;
+  const int grp = lane / kLanes, sub = lane - grp * kLanes;
+  int r, e0, e1;
+  entry_range<kMode>(q, B, S, V, offs, r, e0, e1);
+  const int d = sub * 8;
+  const bool active = d < width;
+  const T* scol = src + d_lo + d;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float csum = 0.f;
+  int nx_row = 0;
+  float nx_coef = 0.f;
+  if (lane < e1 - e0) {
+    nx_row = __ldg(ent_row + e0 + lane);
+    nx_coef = __ldg(ent_coef + e0 + lane);
+  }
+  for (int eb = e0; eb < e1; eb += 32) {
+    const int n = min(32, e1 - eb);
+    const int my_row = nx_row;
+    const float my_coef = nx_coef;  // 0 on the lanes past the batch's end
+    nx_row = 0;
+    nx_coef = 0.f;
+    if (lane < e1 - eb - 32) {  // the next batch, while this one is gathered
+      nx_row = __ldg(ent_row + eb + 32 + lane);
+      nx_coef = __ldg(ent_coef + eb + 32 + lane);
+    }
+    if (kMode == 1) csum += my_coef;
+    for (int j = 0; j < n; j += U * G) {
+      int rr[U];
+      float cc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {  // entry j + u*G + grp (< 32) for this group
+        rr[u] = __shfl_sync(0xFFFFFFFFu, my_row, j + u * G + grp);
+        cc[u] = __shfl_sync(0xFFFFFFFFu, my_coef, j + u * G + grp);
+      }
+      Row8<T> x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (cc[u] != 0.f && active)
+          x[u].load(scol + static_cast<size_t>(rr[u]) * D);
+        else
+          x[u].zero();
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) x[u].fma_into(cc[u], acc);
+    }
+  }
+#pragma unroll
+  for (int o = kLanes; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], o);
+  if (grp == 0 && active) store8<O>(out + static_cast<size_t>(r) * D + d_lo + d, acc);
+  if (kMode == 1 && out_sum != nullptr && d_lo == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xFFFFFFFFu, csum, o);
+    if (lane == 0) out_sum[r] = cvt_out<O>(csum);
+  }
+}
+
 // Register cap for 4 CTAs (32 warps) per SM: the gathers are bound by loads
 // in flight, and 4 resident CTAs measured 28-30% faster than the 3 that the
-// uncapped register count allows.
-template <typename T, typename O, int NC, int kMode>
+// uncapped register count allows. G == 0: full rows in NC passes; G > 0:
+// column slices of slice_w = 256 / G columns.
+template <typename T, typename O, int NC, int G, int U, int kMode>
 __global__ void __launch_bounds__(kGWarps * 32, 4)
     gather_kernel(const T* __restrict__ src, int B, int S, int D, int V, const int* __restrict__ offs,
                   const int* __restrict__ ent_row, const float* __restrict__ ent_coef, int n_rows,
-                  O* __restrict__ out, O* __restrict__ out_sum, unsigned int* row_counter) {
+                  int slice_w, int n_slices, O* __restrict__ out, O* __restrict__ out_sum,
+                  unsigned int* row_counter) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (kMode == 0) {
-    // dH: persistent warps claim rows q = 0, 1, ... from the workspace counter
-    // (the next claim is issued before the current row is gathered). Rows are
-    // position-major (q -> s = q / B, b = q % B): the heavy rows come first
-    // and the empty rows past each sequence's end last.
+    // dH: persistent warps claim items q = 0, 1, ... from the workspace counter
+    // (the next claim is issued before the current one is gathered). Items are
+    // slice-major, then position-major (row q % n_rows -> s = row / B,
+    // b = row % B): the heavy rows come first and the empty rows past each
+    // sequence's end last.
+    const int n_items = n_rows * n_slices;
     int q = 0;
     if (lane == 0) q = static_cast<int>(atomicAdd(row_counter, 1u));
     q = __shfl_sync(0xFFFFFFFFu, q, 0);
-    while (q < n_rows) {
+    while (q < n_items) {
       int qn = 0;
       if (lane == 0) qn = static_cast<int>(atomicAdd(row_counter, 1u));
-      gather_row<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, q, out, out_sum, lane);
+      if constexpr (G == 0) {
+        gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, q, out,
+                                         out_sum, lane);
+      } else {
+        const int sl = q / n_rows;
+        const int d_lo = sl * slice_w;
+        gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+                                            q - sl * n_rows, d_lo, min(slice_w, D - d_lo), out,
+                                            out_sum, lane);
+      }
       q = __shfl_sync(0xFFFFFFFFu, qn, 0);
     }
-  } else {
+  } else if constexpr (G == 0) {
+    // dW: one row per warp.
     const int r = blockIdx.x * kGWarps + warp;
     if (r < n_rows)
-      gather_row<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, out, out_sum, lane);
+      gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, out, out_sum,
+                                       lane);
+  } else {
+    // dW: one (slice, row) per warp; blocks are slice-major (the block scheduler
+    // dispatches them in order).
+    const int per_slice = (n_rows + kGWarps - 1) / kGWarps;
+    const int sl = blockIdx.x / per_slice;
+    const int r = (blockIdx.x - sl * per_slice) * kGWarps + warp;
+    const int d_lo = sl * slice_w;
+    if (r < n_rows)
+      gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, d_lo,
+                                          min(slice_w, D - d_lo), out, out_sum, lane);
   }
 }
 
@@ -468,9 +566,10 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
   return SPARTON_OK;
 }
 
-// Launches one gather_kernel instantiation with a persistent grid: resident
-// CTAs per SM (occupancy API, cached per device) x SMs, capped by the rows.
-template <typename T, typename O, int NC, int kMode>
+// Launches one gather_kernel instantiation: for dH a persistent grid of
+// resident CTAs per SM (occupancy API, cached per device) x SMs, capped by the
+// work; for dW one CTA per kGWarps rows of each slice.
+template <typename T, typename O, int NC, int G, int U, int kMode>
 int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
                      const float* ent_coef, int n_rows, O* out, O* out_sum,
                      unsigned int* row_counter, cudaStream_t stream) {
@@ -485,49 +584,66 @@ int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, 
     std::lock_guard<std::mutex> lock(mu);
     bps = dev < 64 ? per_sm[dev] : 0;
     if (bps == 0) {
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, gather_kernel<T, O, NC, kMode>,
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, gather_kernel<T, O, NC, G, U, kMode>,
                                                         block, 0);
       if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
       if (bps < 1) bps = 1;
       if (dev < 64) per_sm[dev] = bps;
     }
   }
+  const int slice_w = G == 0 ? D : 256 / G;
+  const int n_slices = (D + slice_w - 1) / slice_w;
   // dH rows carry very different amounts of work (bucket sizes, empty rows past
   // each sequence's end): persistent CTAs that claim rows dynamically.
   // dW rows all carry B entries: one CTA per kGWarps rows, balanced by the
   // hardware block scheduler.
-  const long long need = (static_cast<long long>(n_rows) + kGWarps - 1) / kGWarps;
+  const long long need = (static_cast<long long>(n_rows) + kGWarps - 1) / kGWarps * n_slices;
   const long long cap = kMode == 0 ? static_cast<long long>(bps) * device_sm_count() : need;
   const unsigned grid = static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
-  gather_kernel<T, O, NC, kMode><<<grid, block, 0, stream>>>(src, B, S, D, V, offs, ent_row,
-                                                            ent_coef, n_rows, out, out_sum,
-                                                            row_counter);
+  gather_kernel<T, O, NC, G, U, kMode><<<grid, block, 0, stream>>>(
+      src, B, S, D, V, offs, ent_row, ent_coef, n_rows, slice_w, n_slices, out, out_sum,
+      row_counter);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gather_kernel launch");
   return SPARTON_OK;
 }
 
+// Full rows when the gathered working set (col_bytes per column of D) fits the
+// L2 budget, else the widest slice of 256, 128 or 64 columns whose share does
+// (64 at the least).
 template <typename T, typename O, int kMode>
-int launch_gather(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
-                  const float* ent_coef, int n_rows, O* out, O* out_sum,
+int launch_gather(const T* src, long long col_bytes, int B, int S, int D, int V, const int* offs,
+                  const int* ent_row, const float* ent_coef, int n_rows, O* out, O* out_sum,
                   unsigned int* row_counter, cudaStream_t stream) {
+  if (col_bytes * D > kGatherL2Budget && D > 64) {
+    if (D > 256 && col_bytes * 256 <= kGatherL2Budget)
+      return launch_gather_nc<T, O, 1, 1, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+                                                    n_rows, out, out_sum, row_counter, stream);
+    if (D > 128 && col_bytes * 128 <= kGatherL2Budget)
+      return launch_gather_nc<T, O, 1, 2, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+                                                    n_rows, out, out_sum, row_counter, stream);
+    return launch_gather_nc<T, O, 1, 4, 8, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+                                                  out, out_sum, row_counter, stream);
+  }
   if (D <= 256)
-    return launch_gather_nc<T, O, 1, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
-                                            out_sum, row_counter, stream);
+    return launch_gather_nc<T, O, 1, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+                                                  out, out_sum, row_counter, stream);
   if (D <= 512)
-    return launch_gather_nc<T, O, 2, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
-                                            out_sum, row_counter, stream);
+    return launch_gather_nc<T, O, 2, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+                                                  out, out_sum, row_counter, stream);
   if (D <= 768)
-    return launch_gather_nc<T, O, 3, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
-                                            out_sum, row_counter, stream);
-  return launch_gather_nc<T, O, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows, out,
-                                          out_sum, row_counter, stream);
+    return launch_gather_nc<T, O, 3, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+                                                  out, out_sum, row_counter, stream);
+  return launch_gather_nc<T, O, 4, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+                                                out, out_sum, row_counter, stream);
 }
 
 template <typename T, typename O>
 int launch_dh(const void* weight, int B, int S, int D, int V, void* d_hidden,
               const BwdWorkspace& ws, cudaStream_t stream) {
-  return launch_gather<T, O, 0>(static_cast<const T*>(weight), B, S, D, V, ws.offs, ws.perm,
+  // dH gathers rows of W in random order: its working set is all of W.
+  return launch_gather<T, O, 0>(static_cast<const T*>(weight),
+                                static_cast<long long>(V) * sizeof(T), B, S, D, V, ws.offs, ws.perm,
                                 ws.gperm, B * S, static_cast<O*>(d_hidden), nullptr,
                                 ws.row_counter, stream);
 }
@@ -542,7 +658,11 @@ int launch_dw(const void* grad_reps, const void* reps, const int32_t* idx, const
                                                ws.wcoef, ws.status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dw_list_kernel launch");
-  return launch_gather<T, O, 1>(static_cast<const T*>(hidden), B, S, D, V, nullptr, ws.wrow,
+  // dW warps walk the batch rows in step: the working set is the H[b] of the
+  // ~kDwRowsInFlight batch rows they span.
+  return launch_gather<T, O, 1>(static_cast<const T*>(hidden),
+                                static_cast<long long>(kDwRowsInFlight) * S * sizeof(T), B, S, D, V,
+                                nullptr, ws.wrow,
                                 ws.wcoef, V, static_cast<O*>(d_weight), static_cast<O*>(d_bias),
                                 nullptr, stream);
 }

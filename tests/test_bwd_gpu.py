@@ -119,6 +119,34 @@ def test_bwd_matches_oracle(dtype, shape):
         close_to_head(db, head[2], max(rtol, 1e-5), "db vs torch head")
 
 
+# Shapes whose gathered working set exceeds the gathers' 48 MiB L2 budget, so
+# the backward cuts D into column slices (bf16, 2 bytes per element):
+#   dH gathers W rows in random order, working set V * D * 2:
+#     V=40000 -> 256-column slices, V=120000 -> 128, V=250002 -> 64;
+#   dW walks ~16 batch rows in step, working set 16 * S * D * 2:
+#     S=2048, D=1024 -> 256; S=8192, D=512 -> 128; S=16384, D=256 -> 64.
+SLICED = [
+    (2, 32, 768, 40000, (8, 32)),
+    (2, 32, 768, 120000, (8, 32)),
+    (2, 32, 768, 250002, (8, 32)),
+    (3, 2048, 1024, 40, (1000, 2048)),
+    (2, 8192, 512, 40, (4000, 8192)),
+    (2, 16384, 256, 40, (8000, 16384)),
+]
+
+
+@pytest.mark.parametrize("shape", SLICED, ids=lambda s: "B{}S{}D{}V{}".format(*s[:4]))
+def test_bwd_column_slices(shape):
+    B, S, D, V, lengths = shape
+    H, W, b, mask, g = synthetic(B, S, D, V, lengths, dtype=torch.bfloat16, use_bias=True,
+                                 w_std=0.5 / D ** 0.5, seed=B + V)
+    reps, idx, dH, dW, db = run_fwd_bwd(H, W, b, mask, g)
+    ref = orc.backward_from_scores(np64(g), np64(reps), idx.numpy(), np64(H), np64(W), True)
+    close_to_kernel_oracle(dH, ref[0], 1e-2, "dH")
+    close_to_kernel_oracle(dW, ref[1], 1e-2, "dW")
+    close_to_kernel_oracle(db, ref[2], 1e-2, "db")
+
+
 def test_bwd_deterministic_and_zero_where_masked():
     H, W, b, mask, g = synthetic(8, 256, 768, 4000, (32, 256), dtype=torch.bfloat16, seed=9)
     a = run_fwd_bwd(H, W, b, mask, g)
