@@ -9,9 +9,11 @@
 //
 // Here every output element is produced by exactly one warp in a fixed order
 // (deterministic, no atomics):
-//   K2 bwd_sort_kernel   per batch row: stable counting sort of the vocab ids with
-//                        score > 0 by argmax position -> CSR (offs[b][s]) of
-//                        (v, g') pairs, v ascending inside each bucket.
+//   K2 bwd_sort_kernel   per batch row (a cluster of up to 8 CTAs, combined
+//                        through distributed shared memory): stable counting
+//                        sort of the vocab ids with score > 0 by argmax
+//                        position -> CSR (offs[b][s]) of (v, g') pairs, v
+//                        ascending inside each bucket.
 //      dw_list_kernel    tiled transpose of (argmax row, g') to vocab-major
 //                        order: the B entries of each vocab id, contiguous.
 //   K3 gather_kernel<0>  one warp per (b, s) row: dH[b,s,:] = sum over its
@@ -29,6 +31,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
+
+#include <cooperative_groups.h>
 
 #include <mutex>
 #include <type_traits>
@@ -143,39 +147,56 @@ __device__ __forceinline__ void store8(O* p, const float (&x)[8]) {
 }
 
 // ------------------------------------------------------------------ K2: sort
-// One block per batch row, `nw` warps. Warp w owns the contiguous vocab range
-// [w*chunk, (w+1)*chunk) and a row `cnt[w][0..S)` of the shared table.
+// A thread-block cluster of P CTAs (P = 1, 2, 4 or 8) per batch row, `nw`
+// warps each. CTA c of the cluster owns the vocab range [c*part, (c+1)*part)
+// and warp w of it the contiguous sub-range [w*chunk, (w+1)*chunk), with a row
+// `cnt[w][0..S)` of the CTA's shared table.
 //   pass 1: cnt[w][s] = number of entries of warp w with argmax s
-//   scan:   offs[b][s] = exclusive prefix over s of the column sums; then each
-//           cnt[w][s] becomes the first output slot of warp w in bucket s
-//   pass 2: each warp replays its range in order and writes (v, g') at
-//           cnt[w][s] + (rank among lower lanes with the same s) -> stable.
+//   scan:   tot[s] = this CTA's column sum; cnt[w][s] becomes the prefix over
+//           the warps before w. After a cluster barrier every CTA reads all
+//           CTAs' tot[] through distributed shared memory: base[s] = sum over
+//           the CTAs before it, full[s] = sum over all of them (a second
+//           cluster barrier keeps every tot[] alive until all reads are done).
+//           offs[b][s] = exclusive prefix over s of full[]; warp w of CTA c
+//           starts bucket s at offs[b][s] + base[s] + cnt[w][s].
+//   pass 2: each warp replays its range in order and writes (v, g') at its
+//           slot + (rank among lower lanes with the same s) -> stable, v
+//           ascending inside each bucket.
 template <typename T>
 __global__ void __launch_bounds__(1024)
     bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
                     const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
                     int* __restrict__ perm, float* __restrict__ gperm, unsigned int* status,
                     unsigned int* row_counter) {
-  extern __shared__ int cnt[];  // [nw][S]
+  extern __shared__ int cnt[];  // [nw][S], then tot[S] and, when P > 1, base[S], full[S]
   __shared__ int scan_tmp[33];
-  const int b = blockIdx.x;
+  namespace cg = cooperative_groups;
+  const cg::cluster_group cluster = cg::this_cluster();
+  const int P = static_cast<int>(cluster.num_blocks());
+  const int c = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.y;
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (b == 0 && threadIdx.x == 0) {
+  int* tot = cnt + nw * S;
+  int* base = tot + S;
+  int* full = P > 1 ? base + S : tot;
+  if (blockIdx.x == 0 && b == 0 && threadIdx.x == 0) {
     *status = 0u;
     *row_counter = 0u;
   }
   for (int i = threadIdx.x; i < nw * S; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
 
-  const int chunk = (((V + nw - 1) / nw) + 31) & ~31;
-  const int v_begin = warp * chunk;
-  const int v_end = min(V, v_begin + chunk);
+  const int part = (((V + P - 1) / P) + 31) & ~31;
+  const int p_begin = min(V, c * part), p_end = min(V, p_begin + part);
+  const int chunk = (((p_end - p_begin + nw - 1) / nw) + 31) & ~31;
+  const int v_begin = min(p_end, p_begin + warp * chunk);
+  const int v_end = min(p_end, v_begin + chunk);
   const size_t row = static_cast<size_t>(b) * V;
   int* my = cnt + warp * S;
 
-  for (int base = v_begin; base < v_end; base += 32) {
-    const int v = base + lane;
+  for (int vb = v_begin; vb < v_end; vb += 32) {
+    const int v = vb + lane;
     int key = -1;
     if (v < v_end) {
       const float sc = ld_f<T>(reps + row + v);
@@ -187,12 +208,38 @@ __global__ void __launch_bounds__(1024)
   }
   __syncthreads();
 
-  // Exclusive scan over positions of the per-position totals.
+  // This CTA's column sums; each thread owns a contiguous range of positions.
   const int per = (S + blockDim.x - 1) / blockDim.x;
   const int k_begin = min(S, static_cast<int>(threadIdx.x) * per), k_end = min(S, k_begin + per);
+  for (int k = k_begin; k < k_end; ++k) {
+    int run = 0;
+    for (int w = 0; w < nw; ++w) {
+      const int x = cnt[w * S + k];
+      cnt[w * S + k] = run;
+      run += x;
+    }
+    tot[k] = run;
+  }
   int local = 0;
-  for (int k = k_begin; k < k_end; ++k)
-    for (int w = 0; w < nw; ++w) local += cnt[w * S + k];
+  if (P > 1) {
+    cluster.sync();  // every CTA's tot[] is complete
+    for (int k = k_begin; k < k_end; ++k) {
+      int before = 0, all = 0;
+      for (int r = 0; r < P; ++r) {
+        const int x = *cluster.map_shared_rank(tot + k, r);
+        before += r < c ? x : 0;
+        all += x;
+      }
+      base[k] = before;
+      full[k] = all;
+      local += all;
+    }
+    cluster.sync();  // no CTA reads another's tot[] past this point
+  } else {
+    for (int k = k_begin; k < k_end; ++k) local += tot[k];
+  }
+
+  // Exclusive scan over positions of the bucket sizes full[s].
   int incl = local;
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
@@ -213,21 +260,19 @@ __global__ void __launch_bounds__(1024)
   int run = incl - local + (warp > 0 ? scan_tmp[warp - 1] : 0);
   int* orow = offs + static_cast<size_t>(b) * (S + 1);
   for (int k = k_begin; k < k_end; ++k) {
-    orow[k] = run;
-    for (int w = 0; w < nw; ++w) {
-      const int c = cnt[w * S + k];
-      cnt[w * S + k] = run;
-      run += c;
-    }
+    if (c == 0) orow[k] = run;
+    const int start = run + (P > 1 ? base[k] : 0);
+    for (int w = 0; w < nw; ++w) cnt[w * S + k] += start;
+    run += full[k];
   }
-  if (threadIdx.x == 0) orow[S] = scan_tmp[32];
+  if (c == 0 && threadIdx.x == 0) orow[S] = scan_tmp[32];
   __syncthreads();
 
   int* prow = perm + row;
   float* grow = gperm + row;
   const unsigned lt = (1u << lane) - 1u;
-  for (int base = v_begin; base < v_end; base += 32) {
-    const int v = base + lane;
+  for (int vb = v_begin; vb < v_end; vb += 32) {
+    const int v = vb + lane;
     int key = -1;
     float gp = 0.f;
     if (v < v_end) {
@@ -545,23 +590,85 @@ int set_smem(K kernel, int bytes, const char* what) {
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, what);
 }
 
+// Whether clusters of P CTAs with `smem` bytes each can be resident, asked once
+// per (device, P, smem) of the occupancy API and remembered.
+template <typename K>
+bool sort_cluster_fits(K kernel, const cudaLaunchConfig_t* cfg, int P, size_t smem) {
+  struct Entry {
+    int dev, P;
+    size_t smem;
+    bool fits;
+  };
+  static std::mutex mu;
+  static Entry cache[32];
+  static int n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (cache[i].dev == dev && cache[i].P == P && cache[i].smem == smem) return cache[i].fits;
+  int clusters = 0;
+  const bool fits =
+      cudaOccupancyMaxActiveClusters(&clusters, kernel, cfg) == cudaSuccess && clusters >= 1;
+  if (!fits) (void)cudaGetLastError();
+  cache[n < 32 ? n++ : 31] = Entry{dev, P, smem, fits};
+  return fits;
+}
+
+// Cluster size P for the sort: enough CTAs for two per SM (1, 2, 4 or 8 per
+// batch row). Shared memory per CTA: nw warp rows of S counters plus one (P = 1)
+// or three (P > 1) rows, 224 KB at most; long rows that leave fewer than 8
+// warps with P > 1 take P = 1.
+constexpr int kSortSmemInts = 56 * 1024;
+constexpr int kSortMaxS = kSortSmemInts / 2;
+
 template <typename T>
 int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int B, int S, int V,
                 const BwdWorkspace& ws, cudaStream_t stream) {
-  int nw = 49152 / S;
+  if (S > kSortMaxS)
+    return fail(SPARTON_ERR_UNSUPPORTED, "backward supports S <= %d (got %d)", kSortMaxS, S);
+  int P = 1;
+  while (P < 8 && static_cast<long long>(B) * P < 2ll * device_sm_count()) P *= 2;
+  if (P > 1 && kSortSmemInts / S - 3 < 8) P = 1;
+  int nw = kSortSmemInts / S - (P > 1 ? 3 : 1);
   if (nw > 32) nw = 32;
-  if (nw < 1) return fail(SPARTON_ERR_UNSUPPORTED, "backward supports S <= 49152 (got %d)", S);
-  const size_t smem = static_cast<size_t>(nw) * S * sizeof(int);
+  const size_t smem = static_cast<size_t>(nw + (P > 1 ? 3 : 1)) * S * sizeof(int);
   if (smem > 48 * 1024) {
     const int st = set_smem(bwd_sort_kernel<T>, static_cast<int>(smem),
                             "cudaFuncSetAttribute(bwd_sort_kernel)");
     if (st != SPARTON_OK) return st;
   }
-  bwd_sort_kernel<T><<<B, nw * 32, smem, stream>>>(static_cast<const T*>(grad_reps),
-                                                   static_cast<const T*>(reps), idx, S, V,
-                                                   ws.offs, ws.perm, ws.gperm, ws.status,
-                                                   ws.row_counter);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(P), static_cast<unsigned>(B));
+  cfg.blockDim = dim3(static_cast<unsigned>(nw * 32));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(P);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (P > 1 && !sort_cluster_fits(bwd_sort_kernel<T>, &cfg, P, smem)) {
+    // A cluster that cannot be co-scheduled (shared memory, partitioned GPU)
+    // falls back to one CTA per batch row.
+    {
+      P = 1;
+      nw = kSortSmemInts / S - 1;
+      if (nw > 32) nw = 32;
+      cfg.gridDim = dim3(1u, static_cast<unsigned>(B));
+      cfg.blockDim = dim3(static_cast<unsigned>(nw * 32));
+      cfg.dynamicSmemBytes = static_cast<size_t>(nw + 1) * S * sizeof(int);
+      attr[0].val.clusterDim.x = 1;
+    }
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, bwd_sort_kernel<T>, static_cast<const T*>(grad_reps),
+                                           static_cast<const T*>(reps), idx, S, V, ws.offs, ws.perm,
+                                           ws.gperm, ws.status, ws.row_counter);
   if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
   return SPARTON_OK;
 }
