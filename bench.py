@@ -405,7 +405,7 @@ def main(argv=None) -> int:
     import torch.distributed as dist
 
     from sparton_b200 import _lib
-    from sparton_b200.head import VocabShard
+    from sparton_b200.head import VocabShard, row_chunks
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -439,6 +439,7 @@ def main(argv=None) -> int:
     wsb = torch.empty(lib.sparton_bwd_workspace_size(B, S, D, Vs), dtype=torch.uint8, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     dt = _lib.DTYPE[c["dtype"]]
+    chunks = row_chunks(B, S * D * dH.element_size())
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
     def step(k0=None, k1=None):
@@ -458,18 +459,23 @@ def main(argv=None) -> int:
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
                        "bwd")
             return
-        # Sharded: partial dH, its all-reduce (NCCL's stream) overlapping dW / db,
-        # as SpartonHead's sharded backward does.
-        _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
-                                   Wd.data_ptr(), dt, B, S, D, Vs, dH.data_ptr(), None, None,
-                                   _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
-                   "bwd dH")
-        work = dist.all_reduce(dH, group=group, async_op=True)
+        # Sharded, as SpartonHead's sharded backward does: partial dH in chunks of
+        # batch rows, each chunk's all-reduce (NCCL's stream) overlapping the
+        # next chunk, the last ones overlapping dW / db.
+        works = []
+        for b0, b1 in chunks:
+            _lib.check(lib.sparton_bwd(gd[b0:b1].data_ptr(), reps[b0:b1].data_ptr(),
+                                       idx[b0:b1].data_ptr(), Hd[b0:b1].data_ptr(), Wd.data_ptr(),
+                                       dt, b1 - b0, S, D, Vs, dH[b0:b1].data_ptr(), None, None,
+                                       _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
+                       "bwd dH")
+            works.append(dist.all_reduce(dH[b0:b1], group=group, async_op=True))
         _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
                                    Wd.data_ptr(), dt, B, S, D, Vs, None, dW.data_ptr(),
                                    _lib.ptr(db), _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(),
                                    wsb.numel(), sh), "bwd dW")
-        work.wait()
+        for work in works:
+            work.wait()
 
     def barrier():
         if world > 1:
@@ -505,8 +511,9 @@ def main(argv=None) -> int:
     kern_ms = sum(a.elapsed_time(e) for a, e in kern_ev) / args.steps
     kern_ms_max = max_over_ranks(kern_ms)
     # mask_prepare + pack_prepare + forward; backward: sort, dH gather, dW list,
-    # dW gather (db, when there is a bias, is summed inside the dW gather).
-    launches_per_step = 3 + 4
+    # dW gather (db, when there is a bias, is summed inside the dW gather);
+    # sharded, a sort and a dH gather per chunk of batch rows.
+    launches_per_step = 3 + (4 if world == 1 else 2 * len(chunks) + 2)
 
     # ------------------------------------------------------------ end to end
     e2e_ms = None
@@ -537,6 +544,7 @@ def main(argv=None) -> int:
         "config": {"workload": workload_desc(c),
                    "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
                    "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
+                   "dh_allreduce_chunks": len(chunks) if world > 1 else 0,
                    "l2": "flushed (256 MiB write) before every timed step"},
         "tokens_per_s": round(B * S / (step_ms * 1e-3), 1),
         "valid_tokens_per_s": round(T / (step_ms * 1e-3), 1),

@@ -13,7 +13,8 @@ Keyword-only additions (defaults keep the upstream behaviour):
   the kernel's 128-row vocab tile. The forward needs no communication and
   returns ``reps[:, shard]``; the backward all-reduces (sum) the partial
   d_hidden of every rank, in ``grad_reduce_dtype`` (default: fp32 for 16-bit
-  inputs, the input dtype otherwise).
+  inputs, the input dtype otherwise), in chunks of batch rows that overlap
+  the remaining backward kernels.
 * ``gather_output``: with a process group, all-gather the shards so forward
   returns the full ``reps[B, V]``.
 """
@@ -29,6 +30,20 @@ from torch import nn
 from . import ops
 
 VOCAB_TILE = 128
+# The sharded backward all-reduces d_hidden in chunks of batch rows of about
+# this many bytes, each chunk's all-reduce overlapping the next chunk's kernels.
+REDUCE_CHUNK_BYTES = 128 << 20
+
+
+def row_chunks(B: int, row_bytes: int, chunk_bytes: Optional[int] = None) -> list:
+    """Batch-row ranges [(b0, b1), ...] covering [0, B) in chunks of about
+    ``chunk_bytes`` (REDUCE_CHUNK_BYTES by default) of d_hidden, at most 8, as
+    even as the rows allow. Depends only on shapes, so every rank takes the same
+    collective steps."""
+    chunk_bytes = REDUCE_CHUNK_BYTES if chunk_bytes is None else chunk_bytes
+    n = max(1, min(B, 8, (B * row_bytes) // max(chunk_bytes, 1)))
+    cuts = [B * i // n for i in range(n + 1)]
+    return [(a, b) for a, b in zip(cuts, cuts[1:]) if b > a]
 
 
 class VocabShard:
@@ -72,19 +87,30 @@ class _ShardedHead(torch.autograd.Function):
         reps, idx, hidden, weight = ctx.saved_tensors
         need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         need_b = ctx.has_bias and ctx.needs_input_grad[2]
-        # The partial d_hidden first; its all-reduce (on the collective's own
-        # stream) then overlaps the d_weight / d_bias kernels.
-        d_hidden, _, _ = ops.backward_impl(
-            grad_reps, reps, idx, hidden, weight, False, need_hidden=True, need_embed=False,
-            hidden_grad_dtype=ctx.reduce_dtype)
-        # Every rank takes part in the all-reduce, whether or not it needs d_hidden.
-        work = dist.all_reduce(d_hidden, op=dist.ReduceOp.SUM, group=ctx.group, async_op=True)
+        # The partial d_hidden first, in chunks of batch rows: each chunk's
+        # all-reduce (on the collective's own stream) overlaps the kernels of
+        # the next chunk, and the last ones the d_weight / d_bias kernels.
+        # Every rank takes part in the all-reduces, whether or not it needs
+        # d_hidden.
+        B, S, D = hidden.shape
+        rdt = ctx.reduce_dtype
+        grad_c = grad_reps.to(hidden.dtype).contiguous()
+        reps_c, idx_c = reps.contiguous(), idx.contiguous()
+        hidden_c, weight_c = hidden.contiguous(), weight.contiguous()
+        d_hidden = torch.empty((B, S, D), dtype=rdt, device=hidden.device)
+        chunks = row_chunks(B, S * D * d_hidden.element_size())
+        works = []
+        for b0, b1 in chunks:
+            ops.hidden_grad_rows(grad_c, reps_c, idx_c, hidden_c, weight_c, d_hidden, b0, b1)
+            works.append(dist.all_reduce(d_hidden[b0:b1], op=dist.ReduceOp.SUM,
+                                         group=ctx.group, async_op=True))
         d_weight = d_bias = None
         if need_w or need_b:
             _, d_weight, d_bias = ops.backward_impl(
                 grad_reps, reps, idx, hidden, weight, need_b, need_hidden=False,
                 need_embed=need_w)
-        work.wait()
+        for work in works:
+            work.wait()
         return (d_hidden if need_h else None, d_weight if need_w else None,
                 d_bias if need_b else None, None, None, None)
 

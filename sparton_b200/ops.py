@@ -127,6 +127,37 @@ def backward_impl(grad_out: torch.Tensor, scores: torch.Tensor, idx: torch.Tenso
     return d_hidden, d_embed, d_bias
 
 
+def hidden_grad_rows(grad_out: torch.Tensor, scores: torch.Tensor, idx: torch.Tensor,
+                     hidden: torch.Tensor, embed: torch.Tensor, out: torch.Tensor, b0: int,
+                     b1: int, workspace: Optional[torch.Tensor] = None) -> None:
+    """Partial d_hidden of the batch rows [b0, b1) written into ``out[b0:b1]``
+    (``out``: [B, S, D] in hidden's dtype or fp32). The backward's rows are
+    independent, so this is ``sparton_bwd`` on the row slices with only d_hidden
+    requested; the vocab-sharded head uses it to all-reduce finished row
+    chunks while the next chunk is computed. All tensors contiguous, on one
+    device; ``workspace`` (optional) holds at least
+    ``sparton_bwd_workspace_size(b1 - b0, S, D, V)`` bytes."""
+    lib = _lib.load()
+    B, S, D = hidden.shape
+    V = embed.shape[0]
+    _require(0 <= b0 <= b1 <= B, f"bad batch row range [{b0}, {b1}) of {B}")
+    _require(out.shape == (B, S, D) and out.is_contiguous(), "out must be a contiguous [B,S,D]")
+    n = b1 - b0
+    if n == 0:
+        return
+    need = lib.sparton_bwd_workspace_size(n, S, D, V)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=hidden.device)
+    dev = hidden.device
+    with torch.cuda.device(dev):
+        st = lib.sparton_bwd(_lib.ptr(grad_out[b0:b1]), _lib.ptr(scores[b0:b1]),
+                             _lib.ptr(idx[b0:b1]), _lib.ptr(hidden[b0:b1]), _lib.ptr(embed),
+                             _lib.DTYPE[hidden.dtype], n, S, D, V, _lib.ptr(out[b0:b1]), None,
+                             None, _lib.DTYPE[out.dtype], _lib.DTYPE[hidden.dtype],
+                             _lib.ptr(workspace), workspace.numel(), _lib.stream_handle(dev))
+    _lib.check(st, "sparton_bwd (d_hidden rows)")
+
+
 @torch.library.custom_op("sparton::fused_sparton_fwd", mutates_args=())
 def fused_sparton_fwd(hidden: torch.Tensor, embed: torch.Tensor, bias: Optional[torch.Tensor],
                       mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:

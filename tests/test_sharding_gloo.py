@@ -47,14 +47,25 @@ def _cpu_backward(grad_out, scores, idx, hidden, embed, has_bias, need_hidden=Tr
             torch.tensor(db, dtype=embed.dtype) if has_bias else None)
 
 
+def _cpu_hidden_rows(grad_out, scores, idx, hidden, embed, out, b0, b1, workspace=None):
+    dH, _, _ = orc.backward_from_scores(grad_out[b0:b1].numpy(), scores[b0:b1].numpy(),
+                                        idx[b0:b1].numpy(), hidden[b0:b1].detach().numpy(),
+                                        embed.detach().numpy(), False)
+    out[b0:b1] = torch.tensor(dH, dtype=out.dtype)
+
+
 def _worker(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ops.forward_impl = _cpu_forward
         ops.backward_impl = _cpu_backward
+        ops.hidden_grad_rows = _cpu_hidden_rows
         H, W, b, mask, g = _inputs()
         for gather in (False, True):
+            # gather_output=True also runs the d_hidden all-reduce one batch row
+            # per chunk (one collective per chunk, all in flight together).
+            head_mod.REDUCE_CHUNK_BYTES = 1 if gather else 128 << 20
             head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD,
                                gather_output=gather).double()
             head.load({"weight": W, "bias": b})
@@ -92,6 +103,17 @@ def test_vocab_shard_bounds():
             assert all(s.padded % head_mod.VOCAB_TILE == 0 for s in shards)
     tiny = [VocabShard(100, 4, r) for r in range(4)]  # more ranks than tiles: empty shards
     assert [t.size for t in tiny] == [100, 0, 0, 0]
+
+
+def test_row_chunks():
+    assert head_mod.row_chunks(128, 256 * 768 * 4) == [(0, 128)]  # 100 MB: one chunk
+    c = head_mod.row_chunks(64, 1024 * 4096 * 4)  # 1 GB: 8 chunks of 8 rows
+    assert c == [(8 * i, 8 * i + 8) for i in range(8)]
+    c = head_mod.row_chunks(3, 10, chunk_bytes=1)
+    assert c == [(0, 1), (1, 2), (2, 3)]
+    c = head_mod.row_chunks(5, 1 << 30)
+    assert c[0][0] == 0 and c[-1][1] == 5 and all(a < b for a, b in c)
+    assert all(p[1] == q[0] for p, q in zip(c, c[1:]))
 
 
 def test_sharded_head_two_ranks(tmp_path):
