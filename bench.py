@@ -382,6 +382,8 @@ def main(argv=None) -> int:
                     help="BASELINE configuration (default config2, the one the metric is quoted on)")
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of the CPU-baseline sample (default: per workload)")
+    ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
+                    help="stream priority of the NCCL process group (N > 1)")
     ap.add_argument("--legs", default="device,e2e,cpu,losses",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
                          "(training losses on the head's output); profiling runs use --legs device")
@@ -405,13 +407,19 @@ def main(argv=None) -> int:
     import torch.distributed as dist
 
     from sparton_b200 import _lib
-    from sparton_b200.head import VocabShard, row_chunks
+    from sparton_b200.head import VocabShard, _HiddenGradReducer, row_chunks
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        # High-priority NCCL streams: when a d_hidden chunk finishes, its
+        # all-reduce gets SMs ahead of the next chunk's persistent gather kernel,
+        # so the collectives overlap the remaining backward kernels.
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = args.nccl_priority == "high"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev,
+                                pg_options=opts)
         group = dist.group.WORLD
 
     c = WORKLOADS[args.workload]
@@ -432,14 +440,14 @@ def main(argv=None) -> int:
     reps = torch.empty(B, Vs, dtype=c["dtype"], device=dev)
     idx = torch.empty(B, Vs, dtype=torch.int32, device=dev)
     dh_dtype = torch.float32 if world > 1 else c["dtype"]
-    dH = torch.empty(B, S, D, dtype=dh_dtype, device=dev)
+    dH = torch.empty(B, S, D, dtype=c["dtype"], device=dev)  # single GPU; sharded: the reducer's
     dW = torch.empty(Vs, D, dtype=c["dtype"], device=dev)
     db = torch.empty(Vs, dtype=c["dtype"], device=dev) if bd is not None else None
     wsf = torch.empty(lib.sparton_fwd_workspace_size(B, S, D, Vs), dtype=torch.uint8, device=dev)
     wsb = torch.empty(lib.sparton_bwd_workspace_size(B, S, D, Vs), dtype=torch.uint8, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     dt = _lib.DTYPE[c["dtype"]]
-    chunks = row_chunks(B, S * D * dH.element_size())
+    chunks = row_chunks(B, S * D * torch.empty((), dtype=dh_dtype).element_size())
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
     def step(k0=None, k1=None):
@@ -459,23 +467,23 @@ def main(argv=None) -> int:
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
                        "bwd")
             return
-        # Sharded, as SpartonHead's sharded backward does: partial dH in chunks of
-        # batch rows, each chunk's all-reduce (NCCL's stream) overlapping the
-        # next chunk, the last ones overlapping dW / db.
-        works = []
-        for b0, b1 in chunks:
+        # Sharded, with SpartonHead's sharded backward schedule: partial dH in
+        # chunks of batch rows, each chunk all-reduced (fp32, NCCL's stream)
+        # while the next chunk is computed, the last ones overlapping dW / db.
+        red = _HiddenGradReducer(Hd, dh_dtype, group)
+        for b0, b1 in red.chunks:
+            dHp = red.partial
             _lib.check(lib.sparton_bwd(gd[b0:b1].data_ptr(), reps[b0:b1].data_ptr(),
                                        idx[b0:b1].data_ptr(), Hd[b0:b1].data_ptr(), Wd.data_ptr(),
-                                       dt, b1 - b0, S, D, Vs, dH[b0:b1].data_ptr(), None, None,
+                                       dt, b1 - b0, S, D, Vs, dHp[b0:b1].data_ptr(), None, None,
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
                        "bwd dH")
-            works.append(dist.all_reduce(dH[b0:b1], group=group, async_op=True))
+            red.reduce(b0, b1)
         _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
                                    Wd.data_ptr(), dt, B, S, D, Vs, None, dW.data_ptr(),
                                    _lib.ptr(db), _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(),
                                    wsb.numel(), sh), "bwd dW")
-        for work in works:
-            work.wait()
+        red.finish()
 
     def barrier():
         if world > 1:
@@ -545,6 +553,7 @@ def main(argv=None) -> int:
                    "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
                    "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
                    "dh_allreduce_chunks": len(chunks) if world > 1 else 0,
+                   "nccl_stream_priority": args.nccl_priority if world > 1 else None,
                    "l2": "flushed (256 MiB write) before every timed step"},
         "tokens_per_s": round(B * S / (step_ms * 1e-3), 1),
         "valid_tokens_per_s": round(T / (step_ms * 1e-3), 1),

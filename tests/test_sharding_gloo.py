@@ -83,6 +83,21 @@ def _worker(rank, world, port, out_dir):
             np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_dW.npy"), head.weight.grad.numpy())
             np.save(os.path.join(out_dir, f"r{rank}_g{int(gather)}_db.npy"), head.bias.grad.numpy())
             np.save(os.path.join(out_dir, f"r{rank}_shard.npy"), np.array([sh.start, sh.stop]))
+        # float32 hidden states with a float64 reduce dtype: reduce-scatter in
+        # float64, parts rounded to float32, all-gather (one chunk, then one
+        # batch row per chunk).
+        head_mod.REDUCE_SCATTER_GATHER = True
+        for chunk in (128 << 20, 1):
+            head_mod.REDUCE_CHUNK_BYTES = chunk
+            head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD,
+                               grad_reduce_dtype=torch.float64).float()
+            head.load({"weight": W.float(), "bias": b.float()})
+            sh = head.shard
+            hid = H.float().clone().requires_grad_(True)
+            reps = head(hid, mask)
+            reps.backward(g[:, sh.start:sh.stop].float())
+            assert hid.grad.dtype == torch.float32
+            np.save(os.path.join(out_dir, f"r{rank}_rs{int(chunk == 1)}_dH.npy"), hid.grad.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -135,3 +150,12 @@ def test_sharded_head_two_ranks(tmp_path):
                                        rtol=1e-10, atol=1e-12)
             np.testing.assert_allclose(np.load(tmp_path / f"r{r}_g{gather}_db.npy"), db[lo:hi],
                                        rtol=1e-10, atol=1e-12)
+    # reduce-scatter path: float32 hidden states, float32 inputs to the oracle
+    H32, W32, b32, g32 = (t.float().double() for t in (H, W, b, g))
+    reps32, idx32, _ = orc.forward(H32.numpy(), W32.numpy(), b32.numpy(), mask.numpy())
+    dH32, _, _ = orc.backward_from_scores(g32.numpy(), reps32.astype(np.float32), idx32,
+                                          H32.numpy(), W32.numpy(), True)
+    for rows in (0, 1):
+        for r in range(world):
+            np.testing.assert_allclose(np.load(tmp_path / f"r{r}_rs{rows}_dH.npy"), dH32,
+                                       rtol=1e-5, atol=1e-6)
