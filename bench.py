@@ -372,6 +372,70 @@ def run_losses(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
     return out
 
 
+def run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_ranks):
+    """Sparse forms of the head's output for indexing (sparton_b200.sparse), on
+    SPLADE-like reps of the workload's shape [B, V_s] (about half the entries
+    zero), L2 flushed before every iteration, CUDA events, max over ranks:
+    * csr_kernels: sparton_reps_csr with capacity B*V_s (count, scan, fill);
+    * csr_api: sparse.reps_to_csr, which reads nnz back to size its output;
+    * topk: sparton_reps_topk, k = 256.
+    Algorithmic bytes: reps read once plus the output written (CSR: 6 bytes
+    per kept 16-bit entry and the row pointers; top-k: 6 bytes per entry)."""
+    from sparton_b200 import _lib, sparse
+
+    B = c["B"]
+    gen = torch.Generator().manual_seed(11)
+    x = torch.log1p(torch.relu(torch.randn(B, Vs, generator=gen) * 2.0))
+    x[torch.rand(B, Vs, generator=gen) < 0.5] = 0.0
+    reps = x.to(c["dtype"]).to(dev)
+    lib = _lib.load()
+    sh, dt = stream.cuda_stream, _lib.DTYPE[c["dtype"]]
+    es = reps.element_size()
+    crow = torch.empty(B + 1, dtype=torch.int64, device=dev)
+    cols = torch.empty(B * Vs, dtype=torch.int32, device=dev)
+    vals = torch.empty(B * Vs, dtype=c["dtype"], device=dev)
+    ws = torch.empty(max(lib.sparton_sparse_workspace_size(B, Vs), 1), dtype=torch.uint8,
+                     device=dev)
+    k = min(256, Vs)
+    tv = torch.empty(B, k, dtype=c["dtype"], device=dev)
+    ti = torch.empty(B, k, dtype=torch.int32, device=dev)
+
+    def csr_kernels():
+        _lib.check(lib.sparton_reps_csr(reps.data_ptr(), dt, B, Vs, 0.0, crow.data_ptr(),
+                                        cols.data_ptr(), vals.data_ptr(), B * Vs, ws.data_ptr(),
+                                        ws.numel(), sh), "reps_csr")
+
+    def topk():
+        _lib.check(lib.sparton_reps_topk(reps.data_ptr(), dt, B, Vs, k, tv.data_ptr(),
+                                         ti.data_ptr(), sh), "reps_topk")
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        barrier()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        barrier()
+        return max_over_ranks(sum(a.elapsed_time(e) for a, e in evs) / n)
+
+    out = {"shape": [B, Vs], "dtype": str(c["dtype"]).split(".")[-1], "k": k}
+    out["csr_kernels_ms"] = round(timed(csr_kernels), 4)
+    nnz = int(crow[B].item())
+    out["nnz"] = nnz
+    out["csr_algorithmic_bytes"] = B * Vs * es + nnz * (4 + es) + (B + 1) * 8
+    out["csr_gbs"] = round(out["csr_algorithmic_bytes"] / (out["csr_kernels_ms"] * 1e-3) / 1e9, 1)
+    out["csr_api_ms"] = round(timed(lambda: sparse.reps_to_csr(reps)), 4)
+    out["topk_ms"] = round(timed(topk), 4)
+    out["topk_algorithmic_bytes"] = B * Vs * es + B * k * (4 + es)
+    out["topk_gbs"] = round(out["topk_algorithmic_bytes"] / (out["topk_ms"] * 1e-3) / 1e9, 1)
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -384,9 +448,10 @@ def main(argv=None) -> int:
                     help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
                     help="stream priority of the NCCL process group (N > 1)")
-    ap.add_argument("--legs", default="device,e2e,cpu,losses",
+    ap.add_argument("--legs", default="device,e2e,cpu,losses,sparse",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
-                         "(training losses on the head's output); profiling runs use --legs device")
+                         "(training losses on the head's output), sparse (CSR / top-k of "
+                         "reps); profiling runs use --legs device")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -535,6 +600,11 @@ def main(argv=None) -> int:
         losses_out = run_losses(args, c, dev, group, world, Vs, flush, stream, barrier,
                                 max_over_ranks)
 
+    sparse_out = None
+    if "sparse" in legs:
+        sparse_out = run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier,
+                                max_over_ranks)
+
     # ------------------------------------------------------------ report
     peaks, peaks_src = load_peaks()
     fl = nominal_flops(c)
@@ -571,6 +641,7 @@ def main(argv=None) -> int:
             "d2h_bytes_per_step": d2h,
             "path": "SpartonHead forward + autograd backward; pinned host inputs copied in and reps copied out every step, double-buffered on copy streams"},
         "losses": losses_out,
+        "sparse": sparse_out,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }

@@ -205,6 +205,31 @@ int sparton_reg_bwd(const void* reps, const float* colsum, const float* g_l1,
                     const float* g_flops, float scale_l1, float scale_flops, int dtype, int64_t B,
                     int64_t V, void* grad, void* stream);
 
+/* ----------------------------------------------------------- sparse reps */
+/* Sparse forms of the head's output for indexing. Upstream has no counterpart:
+ * its encode (training/model.py:141-144) returns the dense reps, and
+ * training/train.py:205-210 logs the fraction of entries > 0. */
+
+/* Workspace bytes of sparton_reps_csr for reps [B, V]. */
+size_t sparton_sparse_workspace_size(int64_t B, int64_t V);
+
+/* CSR of the entries reps[b, v] > threshold, rows in order, columns ascending
+ * inside each row (torch.Tensor.to_sparse_csr of the thresholded reps):
+ * crow [B + 1] int64 row starts (crow[B] = nnz); cols [capacity] int32 vocab
+ * ids and vals [capacity] (reps' dtype) hold the first `capacity` entries. With
+ * capacity 0 (cols / vals may be NULL) only crow is written: the caller reads
+ * nnz, allocates, and calls again; capacity = B * V always suffices. */
+int sparton_reps_csr(const void* reps, int dtype, int64_t B, int64_t V, float threshold,
+                     int64_t* crow, int32_t* cols, void* vals, int64_t capacity, void* workspace,
+                     size_t workspace_size, void* stream);
+
+/* The k largest entries of every row of reps [B, V], by value descending and,
+ * among equal values, vocab id ascending (NaN above +inf, as torch.topk
+ * orders it): vals [B, k] (reps' dtype), idx [B, k] int32. 0 <= k <= V and
+ * k <= 4096. No workspace. */
+int sparton_reps_topk(const void* reps, int dtype, int64_t B, int64_t V, int64_t k, void* vals,
+                      int32_t* idx, void* stream);
+
 /* --------------------------------------------------------------- status */
 
 /* Copies the device status word of a workspace used by sparton_fwd /

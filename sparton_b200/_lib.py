@@ -43,6 +43,9 @@ EXPORTED_SYMBOLS = (
     "sparton_reg_workspace_size",
     "sparton_reg_fwd",
     "sparton_reg_bwd",
+    "sparton_sparse_workspace_size",
+    "sparton_reps_csr",
+    "sparton_reps_topk",
     "sparton_read_device_status",
 )
 
@@ -82,6 +85,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_reg_fwd.restype = _i
     lib.sparton_reg_bwd.argtypes = [_vp, _vp, _vp, _vp, _f, _f, _i, _i64, _i64, _vp, _vp]
     lib.sparton_reg_bwd.restype = _i
+    lib.sparton_sparse_workspace_size.argtypes = [_i64, _i64]
+    lib.sparton_sparse_workspace_size.restype = _sz
+    lib.sparton_reps_csr.argtypes = [_vp, _i, _i64, _i64, _f, _vp, _vp, _vp, _i64, _vp, _sz, _vp]
+    lib.sparton_reps_csr.restype = _i
+    lib.sparton_reps_topk.argtypes = [_vp, _i, _i64, _i64, _i64, _vp, _vp, _vp]
+    lib.sparton_reps_topk.restype = _i
     lib.sparton_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
     lib.sparton_read_device_status.restype = _i
 

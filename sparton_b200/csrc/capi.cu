@@ -274,4 +274,44 @@ int sparton_reg_bwd(const void* reps, const float* colsum, const float* g_l1,
                         static_cast<cudaStream_t>(stream));
 }
 
+size_t sparton_sparse_workspace_size(int64_t B, int64_t V) {
+  if (B < 0 || V < 0) return 0;
+  return sparse_workspace_bytes(B, V);
+}
+
+int sparton_reps_csr(const void* reps, int dtype, int64_t B, int64_t V, float threshold,
+                     int64_t* crow, int32_t* cols, void* vals, int64_t capacity, void* workspace,
+                     size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_sizes(B, 0, 8, V));
+  SPARTON_TRY(check_dtype(dtype));
+  SPARTON_TRY(check_workspace(workspace, workspace_size, sparse_workspace_bytes(B, V)));
+  if (crow == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "crow is NULL");
+  if (capacity < 0) return fail(SPARTON_ERR_INVALID_ARGUMENT, "negative capacity");
+  if (capacity > 0 && (cols == nullptr || vals == nullptr))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "cols / vals is NULL with capacity %lld",
+                (long long)capacity);
+  if (B * V > 0 && reps == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps is NULL");
+  SPARTON_TRY(check_device());
+  return launch_reps_csr(dtype, reps, static_cast<int>(B), static_cast<int>(V), threshold, crow,
+                         cols, vals, capacity, sparse_workspace_carve(workspace, B, V),
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sparton_reps_topk(const void* reps, int dtype, int64_t B, int64_t V, int64_t k, void* vals,
+                      int32_t* idx, void* stream) {
+  SPARTON_TRY(check_sizes(B, 0, 8, V));
+  SPARTON_TRY(check_dtype(dtype));
+  if (k < 0 || k > V)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "k=%lld must lie in [0, V=%lld]", (long long)k,
+                (long long)V);
+  if (k > kTopkMax)
+    return fail(SPARTON_ERR_UNSUPPORTED, "k=%lld above the supported %d", (long long)k, kTopkMax);
+  if (B * k == 0) return SPARTON_OK;
+  if (reps == nullptr || vals == nullptr || idx == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps / vals / idx is NULL");
+  SPARTON_TRY(check_device());
+  return launch_reps_topk(dtype, reps, static_cast<int>(B), static_cast<int>(V),
+                          static_cast<int>(k), vals, idx, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -164,6 +164,21 @@ int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float
                    const float* g_flops, float scale_l1, float scale_flops, int B, int V,
                    void* grad, cudaStream_t stream);
 
+// Sparse forms of reps (sparse.cu): CSR of the entries above a threshold and
+// the per-row top-k.
+struct SparseWorkspace {
+  int* chunk_cnt;  // [B][ceil(V / 4096)] entries above the threshold per chunk
+  int* chunk_off;  // the same, exclusive prefix in row-major order
+};
+constexpr int kTopkMax = 4096;
+size_t sparse_workspace_bytes(int64_t B, int64_t V);
+SparseWorkspace sparse_workspace_carve(void* base, int64_t B, int64_t V);
+int launch_reps_csr(int dtype, const void* reps, int B, int V, float threshold, int64_t* crow,
+                    int32_t* cols, void* vals, int64_t capacity, const SparseWorkspace& ws,
+                    cudaStream_t stream);
+int launch_reps_topk(int dtype, const void* reps, int B, int V, int k, void* vals, int32_t* idx,
+                     cudaStream_t stream);
+
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,
                void* d_hidden, void* d_weight, void* d_bias, int d_hidden_dtype,
