@@ -124,12 +124,20 @@ struct Row8<float> {
   }
 };
 
-// Eight fp32 values stored as eight elements of O (one 16-byte store for 16-bit O).
-template <typename O>
+// Eight fp32 values stored as eight elements of O (one 16-byte store for 16-bit O);
+// kStream: evict-first stores (st.global.cs), which do not displace data the
+// kernel still gathers.
+template <typename O, bool kStream = false>
 __device__ __forceinline__ void store8(O* p, const float (&x)[8]) {
   if constexpr (std::is_same<O, float>::value) {
-    reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
-    reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    const float4 a = make_float4(x[0], x[1], x[2], x[3]), b = make_float4(x[4], x[5], x[6], x[7]);
+    if constexpr (kStream) {
+      __stcs(reinterpret_cast<float4*>(p), a);
+      __stcs(reinterpret_cast<float4*>(p) + 1, b);
+    } else {
+      reinterpret_cast<float4*>(p)[0] = a;
+      reinterpret_cast<float4*>(p)[1] = b;
+    }
   } else {
     uint32_t w[4];
 #pragma unroll
@@ -142,7 +150,11 @@ __device__ __forceinline__ void store8(O* p, const float (&x)[8]) {
         memcpy(&w[i], &h, 4);
       }
     }
-    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    const uint4 u = make_uint4(w[0], w[1], w[2], w[3]);
+    if constexpr (kStream)
+      __stcs(reinterpret_cast<uint4*>(p), u);
+    else
+      *reinterpret_cast<uint4*>(p) = u;
   }
 }
 
@@ -360,6 +372,24 @@ __global__ void __launch_bounds__(256)
 // batch is prefetched while the current one is gathered.
 constexpr int kGWarps = 8;
 constexpr int kGUnroll = 4;
+// Sliced gathers: the entry lists are read once per slice and the outputs
+// written once, so both go through L2 evict-first (ld/st .cs) and leave it to
+// the slice of src, which is gathered many times.
+#ifndef SPARTON_SLICE_STREAM_LISTS
+#define SPARTON_SLICE_STREAM_LISTS 1
+#endif
+#ifndef SPARTON_SLICE_STREAM_STORES
+#define SPARTON_SLICE_STREAM_STORES 1
+#endif
+constexpr bool kSliceStreamStores = SPARTON_SLICE_STREAM_STORES != 0;
+template <typename X>
+__device__ __forceinline__ X ld_list(const X* p) {
+#if SPARTON_SLICE_STREAM_LISTS
+  return __ldcs(p);
+#else
+  return __ldg(p);
+#endif
+}
 // Bytes of gathered data that are expected to stay resident in the 126 MB L2
 // next to the other traffic of the kernel, and the batch rows that the dW
 // warps in flight span.
@@ -471,8 +501,8 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
   int nx_row = 0;
   float nx_coef = 0.f;
   if (lane < e1 - e0) {
-    nx_row = __ldg(ent_row + e0 + lane);
-    nx_coef = __ldg(ent_coef + e0 + lane);
+    nx_row = ld_list(ent_row + e0 + lane);
+    nx_coef = ld_list(ent_coef + e0 + lane);
   }
   for (int eb = e0; eb < e1; eb += 32) {
     const int n = min(32, e1 - eb);
@@ -481,8 +511,8 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
     nx_row = 0;
     nx_coef = 0.f;
     if (lane < e1 - eb - 32) {  // the next batch, while this one is gathered
-      nx_row = __ldg(ent_row + eb + 32 + lane);
-      nx_coef = __ldg(ent_coef + eb + 32 + lane);
+      nx_row = ld_list(ent_row + eb + 32 + lane);
+      nx_coef = ld_list(ent_coef + eb + 32 + lane);
     }
     if (kMode == 1) csum += my_coef;
     for (int j = 0; j < n; j += U * G) {
@@ -509,7 +539,7 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
   for (int o = kLanes; o < 32; o <<= 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], o);
-  if (grp == 0 && active) store8<O>(out + static_cast<size_t>(r) * D + d_lo + d, acc);
+  if (grp == 0 && active) store8<O, kSliceStreamStores>(out + static_cast<size_t>(r) * D + d_lo + d, acc);
   if (kMode == 1 && out_sum != nullptr && d_lo == 0) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xFFFFFFFFu, csum, o);
