@@ -436,6 +436,84 @@ def run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
     return out
 
 
+def run_transform(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_ranks):
+    """The MLM transform in front of the head (sparton_b200.transform) at the
+    workload's shape, L2 flushed before every iteration, CUDA events, max over
+    ranks (single GPU: the projection's head is unsharded):
+    * kernels_fwd / kernels_bwd: sparton_transform_fwd / _bwd alone (gelu +
+      LayerNorm, and its backward with the d_gamma / d_beta / d_bias sums);
+    * projection: SpartonProjection forward + backward (dense GEMMs on cuBLAS,
+      the transform kernels, the head), against
+    * projection_torch_transform: the same with the transform as torch modules
+      (nn.Linear, gelu, nn.LayerNorm: the reference's ProjectionSparton path).
+    Algorithmic bytes of the transform kernels: forward reads y and writes h
+    (2·B·S·D·2); backward reads dh and y and writes dy in the row kernel, and
+    reads dh, y, dy in the column kernel (6·B·S·D·2)."""
+    from torch import nn
+
+    from sparton_b200 import transform as tr
+
+    B, S, D, V = c["B"], c["S"], c["D"], c["V"]
+    dt = c["dtype"]
+    gen = torch.Generator().manual_seed(13)
+    x = torch.randn(B, S, D, generator=gen).to(dt).to(dev)
+    y = (torch.randn(B, S, D, generator=gen) * 1.5).to(dt).to(dev)
+    gamma = torch.ones(D, dtype=dt, device=dev)
+    beta = torch.zeros(D, dtype=dt, device=dev)
+    dh = torch.randn(B, S, D, generator=gen).to(dt).to(dev)
+    _, mean, rstd = tr.transform_fwd_impl(y, gamma, beta, 1e-12)
+
+    dense = nn.Linear(D, D).to(dev, dt)
+    ln = nn.LayerNorm(D, eps=1e-12).to(dev, dt)
+    decoder = nn.Linear(D, V, bias=c["bias"]).to(dev, dt)
+
+    class Transform(nn.Module):  # the reference's RobertaTransform layout
+        def __init__(self):
+            super().__init__()
+            self.dense, self.layer_norm = dense, ln
+
+        def forward(self, t):
+            return self.layer_norm(torch.nn.functional.gelu(self.dense(t)))
+
+    ref_t = Transform()
+    proj = tr.SpartonProjection(ref_t, decoder)
+    mask = make_inputs(c)[3].to(dev)
+    g = torch.randn(B, V, generator=gen).to(dt).to(dev)
+
+    def projection():
+        xi = x.detach().requires_grad_(True)
+        proj(xi, mask).backward(g)
+
+    def projection_torch_transform():
+        xi = x.detach().requires_grad_(True)
+        proj.sparton_head(ref_t(xi), mask).backward(g)
+
+    def timed(fn, n=10):
+        for _ in range(3):
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        barrier()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        barrier()
+        return max_over_ranks(sum(a.elapsed_time(e) for a, e in evs) / n)
+
+    es = torch.empty((), dtype=dt).element_size()
+    out = {"shape": [B, S, D], "dtype": str(dt).split(".")[-1]}
+    out["kernels_fwd_ms"] = round(timed(lambda: tr.transform_fwd_impl(y, gamma, beta, 1e-12)), 4)
+    out["kernels_bwd_ms"] = round(timed(lambda: tr.transform_bwd_impl(dh, y, gamma, mean, rstd)), 4)
+    out["kernels_fwd_gbs"] = round(2 * B * S * D * es / (out["kernels_fwd_ms"] * 1e-3) / 1e9, 1)
+    out["kernels_bwd_gbs"] = round(6 * B * S * D * es / (out["kernels_bwd_ms"] * 1e-3) / 1e9, 1)
+    if world == 1:
+        out["projection_fwd_bwd_ms"] = round(timed(projection), 4)
+        out["projection_torch_transform_fwd_bwd_ms"] = round(timed(projection_torch_transform), 4)
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -448,10 +526,11 @@ def main(argv=None) -> int:
                     help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
                     help="stream priority of the NCCL process group (N > 1)")
-    ap.add_argument("--legs", default="device,e2e,cpu,losses,sparse",
+    ap.add_argument("--legs", default="device,e2e,cpu,losses,sparse,transform",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
                          "(training losses on the head's output), sparse (CSR / top-k of "
-                         "reps); profiling runs use --legs device")
+                         "reps), transform (MLM transform before the head); profiling runs "
+                         "use --legs device")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -605,6 +684,11 @@ def main(argv=None) -> int:
         sparse_out = run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier,
                                 max_over_ranks)
 
+    transform_out = None
+    if "transform" in legs:
+        transform_out = run_transform(args, c, dev, group, world, Vs, flush, stream, barrier,
+                                      max_over_ranks)
+
     # ------------------------------------------------------------ report
     peaks, peaks_src = load_peaks()
     fl = nominal_flops(c)
@@ -642,6 +726,7 @@ def main(argv=None) -> int:
             "path": "SpartonHead forward + autograd backward; pinned host inputs copied in and reps copied out every step, double-buffered on copy streams"},
         "losses": losses_out,
         "sparse": sparse_out,
+        "transform": transform_out,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }

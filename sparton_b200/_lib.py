@@ -46,6 +46,9 @@ EXPORTED_SYMBOLS = (
     "sparton_sparse_workspace_size",
     "sparton_reps_csr",
     "sparton_reps_topk",
+    "sparton_transform_fwd",
+    "sparton_transform_workspace_size",
+    "sparton_transform_bwd",
     "sparton_read_device_status",
 )
 
@@ -91,6 +94,13 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_reps_csr.restype = _i
     lib.sparton_reps_topk.argtypes = [_vp, _i, _i64, _i64, _i64, _vp, _vp, _vp]
     lib.sparton_reps_topk.restype = _i
+    lib.sparton_transform_fwd.argtypes = [_vp, _vp, _vp, _f, _i, _i64, _i64, _vp, _vp, _vp, _vp]
+    lib.sparton_transform_fwd.restype = _i
+    lib.sparton_transform_workspace_size.argtypes = [_i64, _i64]
+    lib.sparton_transform_workspace_size.restype = _sz
+    lib.sparton_transform_bwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _vp, _vp, _vp,
+                                          _vp, _vp, _sz, _vp]
+    lib.sparton_transform_bwd.restype = _i
     lib.sparton_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
     lib.sparton_read_device_status.restype = _i
 

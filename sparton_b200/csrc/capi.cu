@@ -314,4 +314,56 @@ int sparton_reps_topk(const void* reps, int dtype, int64_t B, int64_t V, int64_t
                           static_cast<int>(k), vals, idx, static_cast<cudaStream_t>(stream));
 }
 
+size_t sparton_transform_workspace_size(int64_t rows, int64_t D) {
+  if (rows < 0 || D < 0) return 0;
+  return transform_workspace_bytes(rows, D);
+}
+
+int sparton_transform_fwd(const void* y, const void* gamma, const void* beta, float eps, int dtype,
+                          int64_t rows, int64_t D, void* h, float* mean, float* rstd,
+                          void* stream) {
+  SPARTON_TRY(check_dtype(dtype));
+  if (rows < 0 || D < 1 || rows > (1ll << 31) - 1 || D > (1 << 16) || rows * D > (1ll << 40))
+    return fail(SPARTON_ERR_UNSUPPORTED, "sizes out of range (rows=%lld D=%lld)",
+                (long long)rows, (long long)D);
+  if (rows == 0) return SPARTON_OK;
+  if (y == nullptr || gamma == nullptr || beta == nullptr || h == nullptr || mean == nullptr ||
+      rstd == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "a pointer argument is NULL");
+  if (!(eps >= 0.f)) return fail(SPARTON_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  SPARTON_TRY(check_device());
+  return launch_transform_fwd(dtype, y, gamma, beta, eps, static_cast<int>(rows),
+                              static_cast<int>(D), h, mean, rstd,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, const float* mean,
+                          const float* rstd, int dtype, int64_t rows, int64_t D, void* dy,
+                          void* d_gamma, void* d_beta, void* d_bias, void* workspace,
+                          size_t workspace_size, void* stream) {
+  SPARTON_TRY(check_dtype(dtype));
+  if (rows < 0 || D < 1 || rows > (1ll << 31) - 1 || D > (1 << 16) || rows * D > (1ll << 40))
+    return fail(SPARTON_ERR_UNSUPPORTED, "sizes out of range (rows=%lld D=%lld)",
+                (long long)rows, (long long)D);
+  const bool cols = d_gamma != nullptr || d_beta != nullptr || d_bias != nullptr;
+  if (cols) SPARTON_TRY(check_workspace(workspace, workspace_size, transform_workspace_bytes(rows, D)));
+  if (rows == 0) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t es = dtype == SPARTON_DTYPE_F32 ? 4 : 2;
+    for (void* p : {d_gamma, d_beta, d_bias})
+      if (p != nullptr) {
+        const cudaError_t e = cudaMemsetAsync(p, 0, static_cast<size_t>(D) * es, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+      }
+    return SPARTON_OK;
+  }
+  if (dh == nullptr || y == nullptr || gamma == nullptr || mean == nullptr || rstd == nullptr ||
+      dy == nullptr)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "a pointer argument is NULL");
+  SPARTON_TRY(check_device());
+  return launch_transform_bwd(dtype, dh, y, gamma, mean, rstd, static_cast<int>(rows),
+                              static_cast<int>(D), dy, d_gamma, d_beta, d_bias, workspace,
+                              static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

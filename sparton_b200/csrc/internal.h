@@ -179,6 +179,15 @@ int launch_reps_csr(int dtype, const void* reps, int B, int V, float threshold, 
 int launch_reps_topk(int dtype, const void* reps, int B, int V, int k, void* vals, int32_t* idx,
                      cudaStream_t stream);
 
+// MLM transform, GELU + LayerNorm part (transform.cu).
+size_t transform_workspace_bytes(int64_t rows, int64_t D);
+int launch_transform_fwd(int dtype, const void* y, const void* gamma, const void* beta, float eps,
+                         int rows, int D, void* h, float* mean, float* rstd, cudaStream_t stream);
+int launch_transform_bwd(int dtype, const void* dh, const void* y, const void* gamma,
+                         const float* mean, const float* rstd, int rows, int D, void* dy,
+                         void* d_gamma, void* d_beta, void* d_bias, void* workspace,
+                         cudaStream_t stream);
+
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,
                void* d_hidden, void* d_weight, void* d_bias, int d_hidden_dtype,

@@ -17,10 +17,10 @@ DTYPES = {"float64": torch.float64, "float32": torch.float32, "bfloat16": torch.
 
 
 def golden_names():
-    """The head's fixtures (the loss and sparse-form fixtures, losses_*.npz and
-    sparse_*.npz, have their own tests)."""
+    """The head's fixtures (the loss, sparse-form and transform fixtures,
+    losses_*.npz, sparse_*.npz and transform_*.npz, have their own tests)."""
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith(("losses_", "sparse_")))
+                  if not os.path.basename(p).startswith(("losses_", "sparse_", "transform_")))
 
 
 def load_golden(name: str) -> dict:
