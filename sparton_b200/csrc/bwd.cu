@@ -620,34 +620,6 @@ int set_smem(K kernel, int bytes, const char* what) {
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, what);
 }
 
-// Whether clusters of P CTAs with `smem` bytes each can be resident, asked once
-// per (device, P, smem) of the occupancy API and remembered.
-template <typename K>
-bool sort_cluster_fits(K kernel, const cudaLaunchConfig_t* cfg, int P, size_t smem) {
-  struct Entry {
-    int dev, P;
-    size_t smem;
-    bool fits;
-  };
-  static std::mutex mu;
-  static Entry cache[32];
-  static int n = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return false;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  for (int i = 0; i < n; ++i)
-    if (cache[i].dev == dev && cache[i].P == P && cache[i].smem == smem) return cache[i].fits;
-  int clusters = 0;
-  const bool fits =
-      cudaOccupancyMaxActiveClusters(&clusters, kernel, cfg) == cudaSuccess && clusters >= 1;
-  if (!fits) (void)cudaGetLastError();
-  cache[n < 32 ? n++ : 31] = Entry{dev, P, smem, fits};
-  return fits;
-}
-
 // Cluster size P for the sort: enough CTAs for two per SM (1, 2, 4 or 8 per
 // batch row). Shared memory per CTA: nw warp rows of S counters plus one (P = 1)
 // or three (P > 1) rows, 224 KB at most; long rows that leave fewer than 8
@@ -683,7 +655,7 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (P > 1 && !sort_cluster_fits(bwd_sort_kernel<T>, &cfg, P, smem)) {
+  if (P > 1 && !cluster_fits(bwd_sort_kernel<T>, &cfg, P, smem)) {
     // A cluster that cannot be co-scheduled (shared memory, partitioned GPU)
     // falls back to one CTA per batch row.
     {

@@ -4,6 +4,8 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -178,6 +180,34 @@ int launch_reps_csr(int dtype, const void* reps, int B, int V, float threshold, 
                     cudaStream_t stream);
 int launch_reps_topk(int dtype, const void* reps, int B, int V, int k, void* vals, int32_t* idx,
                      cudaStream_t stream);
+
+// Whether clusters of P CTAs with `smem` bytes each can be resident, asked once
+// per (device, P, smem) of the occupancy API and remembered.
+template <typename K>
+inline bool cluster_fits(K kernel, const cudaLaunchConfig_t* cfg, int P, size_t smem) {
+  struct Entry {
+    int dev, P;
+    size_t smem;
+    bool fits;
+  };
+  static std::mutex mu;
+  static Entry cache[32];
+  static int n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (cache[i].dev == dev && cache[i].P == P && cache[i].smem == smem) return cache[i].fits;
+  int clusters = 0;
+  const bool fits =
+      cudaOccupancyMaxActiveClusters(&clusters, kernel, cfg) == cudaSuccess && clusters >= 1;
+  if (!fits) (void)cudaGetLastError();
+  cache[n < 32 ? n++ : 31] = Entry{dev, P, smem, fits};
+  return fits;
+}
 
 // MLM transform, GELU + LayerNorm part (transform.cu).
 size_t transform_workspace_bytes(int64_t rows, int64_t D);

@@ -15,14 +15,17 @@
 //                     chunk_off + rank: columns ascending inside every row.
 //                     Entries at or past `capacity` are not written (the
 //                     caller sees nnz in crow[B]).
-// Top-k, one CTA per row:
+// Top-k, a cluster of up to 8 CTAs per row (enough CTAs for two per SM):
 //   radix select on order-preserving unsigned keys (8 bits a pass: 2 passes
-//   for 16-bit types, 4 for fp32) finds the k-th largest key K and how many
-//   of its equals to take; one ordered pass collects the entries above K and
-//   the first such equals in vocab order; a bitonic sort in shared memory
-//   orders the k by (value descending, vocab id ascending).
+//   for 16-bit types, 4 for fp32), the CTAs' histograms summed through
+//   distributed shared memory, finds the k-th largest key K and how many of
+//   its equals to take; one ordered pass collects the entries above K and the
+//   first such equals in vocab order into CTA 0; a bitonic sort in its shared
+//   memory orders the k by (value descending, vocab id ascending).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <cooperative_groups.h>
 
 #include "internal.h"
 
@@ -202,7 +205,9 @@ __global__ void __launch_bounds__(kCsrThreads)
 }
 
 // ------------------------------------------------------------------ top-k
-// Shared memory: hist[256], then k_pad (key, id) pairs for the sort.
+// A thread-block cluster of P CTAs per row (P = 1 .. 8); CTA c walks the vocab
+// range [c*part, (c+1)*part). Shared memory: hist[256], then k_pad (key, id)
+// pairs (used in CTA 0).
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads)
     topk_kernel(const T* __restrict__ reps, int V, int k, int k_pad, T* __restrict__ out_vals,
@@ -212,19 +217,26 @@ __global__ void __launch_bounds__(kTopkThreads)
   uint32_t* skey = smem + 256;      // [k_pad]
   int32_t* sid = reinterpret_cast<int32_t*>(skey + k_pad);  // [k_pad]
   __shared__ int tmp[32];
-  __shared__ uint32_t s_prefix, s_remaining, s_gt;
-  const int b = blockIdx.x;
+  __shared__ uint32_t s_prefix, s_remaining, s_eq_before, s_gt;
+  namespace cg = cooperative_groups;
+  const cg::cluster_group cluster = cg::this_cluster();
+  const int P = static_cast<int>(cluster.num_blocks());
+  const int c = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.y;
   const T* row = reps + static_cast<size_t>(b) * V;
+  const int part = (((V + P - 1) / P) + 31) & ~31;
+  const int v_lo = min(V, c * part), v_hi = min(V, v_lo + part);
   constexpr int kBits = Key<T>::kBits;
-
   // Each warp takes kTileU*32 consecutive entries per step (entry
   // base + u*32 + lane), all kTileU loads of a lane issued first.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int kStep = kTopkThreads * kTileU;
+  if (threadIdx.x == 0) s_gt = 0;
 
-  // Radix select: after the pass on bits [shift, shift+8), `prefix` holds the
-  // top bits of K and `remaining` how many elements with that prefix still
-  // belong to the top k.
+  // Radix select over the whole row: after the pass on bits [shift, shift+8),
+  // `prefix` holds the top bits of K and `remaining` how many elements with
+  // that prefix still belong to the top k. Every CTA sums the cluster's
+  // histograms itself (distributed shared memory) and picks the same digit.
   uint32_t prefix = 0, prefix_mask = 0;
   uint32_t remaining = static_cast<uint32_t>(k);
   for (int shift = kBits - 8; shift >= 0; shift -= 8) {
@@ -232,67 +244,76 @@ __global__ void __launch_bounds__(kTopkThreads)
     __syncthreads();
     // Warp-aggregated counts: most entries of a SPLADE row share one value
     // (0), so the lanes with the same digit add once.
-    for (int base = warp * 32 * kTileU; base < V; base += kStep) {
+    for (int base = v_lo + warp * 32 * kTileU; base < v_hi; base += kStep) {
       uint32_t key[kTileU];
 #pragma unroll
       for (int u = 0; u < kTileU; ++u) {
         const int v = base + u * 32 + lane;
-        key[u] = v < V ? Key<T>::of(row + v) : 0u;
+        key[u] = v < v_hi ? Key<T>::of(row + v) : 0u;
       }
 #pragma unroll
       for (int u = 0; u < kTileU; ++u) {
         const int v = base + u * 32 + lane;
         const uint32_t d =
-            (v < V && (key[u] & prefix_mask) == prefix) ? (key[u] >> shift) & 0xFFu : 256u;
+            (v < v_hi && (key[u] & prefix_mask) == prefix) ? (key[u] >> shift) & 0xFFu : 256u;
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, d);
         if (d < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
       }
     }
-    __syncthreads();
+    cluster.sync();  // every CTA's histogram is complete
     // Digits in descending order, one per thread: the digit whose bucket
     // holds the remaining-th largest key of the prefix group.
     const int t = static_cast<int>(threadIdx.x);
-    const uint32_t own = t < 256 ? hist[255 - t] : 0u;
+    uint32_t own = 0, before = 0;
+    if (t < 256) {
+      for (int r = 0; r < P; ++r) {
+        const uint32_t x = *cluster.map_shared_rank(hist + (255 - t), r);
+        own += x;
+        before += r < c ? x : 0u;
+      }
+    }
     int total;
     const uint32_t above = static_cast<uint32_t>(block_excl_scan(static_cast<int>(own), tmp, total));
     if (t < 256 && above < remaining && above + own >= remaining) {
       s_prefix = prefix | (static_cast<uint32_t>(255 - t) << shift);
       s_remaining = remaining - above;
+      s_eq_before = before;  // after the last pass: equals of K in the CTAs before this one
     }
-    __syncthreads();
+    cluster.sync();  // no CTA reads another's histogram past this point
     prefix = s_prefix;
     remaining = s_remaining;
     prefix_mask |= 0xFFu << shift;
-    __syncthreads();
   }
   // K = prefix (all bits); take every key > K and the first `remaining`
-  // equals in vocab order (rank = equals before the entry: in earlier warps'
-  // spans of the step, then earlier u, then lower lanes).
+  // equals in vocab order (rank = equals in earlier CTAs, then in earlier
+  // warps' spans of the step, then earlier u, then lower lanes), written into
+  // CTA 0's shared memory.
   const uint32_t K = prefix;
-  if (threadIdx.x == 0) s_gt = 0;
-  __syncthreads();
   const int n_gt = k - static_cast<int>(remaining);
+  uint32_t* dkey = cluster.map_shared_rank(skey, 0);
+  int32_t* did = cluster.map_shared_rank(sid, 0);
+  uint32_t* dgt = cluster.map_shared_rank(&s_gt, 0);
   const unsigned lt = (1u << lane) - 1u;
-  int eq_seen = 0;
-  for (int base0 = 0; base0 < V; base0 += kStep) {
+  int eq_seen = static_cast<int>(s_eq_before);
+  for (int base0 = v_lo; base0 < v_hi; base0 += kStep) {
     const int base = base0 + warp * 32 * kTileU;
     uint32_t key[kTileU];
 #pragma unroll
     for (int u = 0; u < kTileU; ++u) {
       const int v = base + u * 32 + lane;
-      key[u] = v < V ? Key<T>::of(row + v) : 0u;
+      key[u] = v < v_hi ? Key<T>::of(row + v) : 0u;
     }
     unsigned eqm[kTileU];
     int warp_eq = 0;
 #pragma unroll
     for (int u = 0; u < kTileU; ++u) {
       const int v = base + u * 32 + lane;
-      eqm[u] = __ballot_sync(0xFFFFFFFFu, v < V && key[u] == K);
+      eqm[u] = __ballot_sync(0xFFFFFFFFu, v < v_hi && key[u] == K);
       warp_eq += __popc(eqm[u]);
-      if (v < V && key[u] > K) {
-        const uint32_t at = atomicAdd(&s_gt, 1u);
-        skey[at] = key[u];
-        sid[at] = v;
+      if (v < v_hi && key[u] > K) {
+        const uint32_t at = atomicAdd(dgt, 1u);
+        dkey[at] = key[u];
+        did[at] = v;
       }
     }
     int total;
@@ -303,14 +324,16 @@ __global__ void __launch_bounds__(kTopkThreads)
       if ((eqm[u] >> lane) & 1u) {
         const int r = rank + __popc(eqm[u] & lt);
         if (r < static_cast<int>(remaining)) {
-          skey[n_gt + r] = key[u];
-          sid[n_gt + r] = base + u * 32 + lane;
+          dkey[n_gt + r] = key[u];
+          did[n_gt + r] = base + u * 32 + lane;
         }
       }
       rank += __popc(eqm[u]);
     }
     eq_seen += total;
   }
+  cluster.sync();  // CTA 0 holds all k candidates
+  if (c != 0) return;
   for (int i = k + static_cast<int>(threadIdx.x); i < k_pad; i += kTopkThreads) {
     skey[i] = 0;  // below every real key in the descending order
     sid[i] = 0x7FFFFFFF;
@@ -385,9 +408,31 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(topk_kernel)");
   }
-  topk_kernel<T><<<B, kTopkThreads, smem, stream>>>(static_cast<const T*>(reps), V, k, k_pad,
-                                                    static_cast<T*>(vals), idx);
-  const cudaError_t e = cudaGetLastError();
+  // Enough CTAs for two per SM, each walking at least 16384 entries of its
+  // row (shorter spans lose more to the cluster barriers than they gain:
+  // [128, 30522] ran 50 µs with one CTA per row, 59 µs with two).
+  int P = 1;
+  while (P < 8 && static_cast<long long>(B) * P < 2ll * device_sm_count() &&
+         V / (2 * P) >= 16384)
+    P *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(P), static_cast<unsigned>(B));
+  cfg.blockDim = dim3(kTopkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(P);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (P > 1 && !cluster_fits(topk_kernel<T>, &cfg, P, smem)) {
+    cfg.gridDim = dim3(1u, static_cast<unsigned>(B));
+    attr[0].val.clusterDim.x = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel<T>, static_cast<const T*>(reps), V,
+                                           k, k_pad, static_cast<T*>(vals), idx);
   if (e != cudaSuccess) return cuda_fail(e, "topk_kernel launch");
   return SPARTON_OK;
 }
