@@ -8,11 +8,11 @@ gradients of hidden, decoder weight and bias) are saved as ``<case>.npz``
 together with the inputs, and pin the numpy oracle in ``oracle/`` before the
 tests trust it.
 
-This script needs the reference checkout (``--reference``, default
-``/root/reference``), which exists only where the fixtures are made; the
+This script needs a checkout of the reference (``--reference PATH``, the
+project root of hhkbble/sparton), which exists only where the fixtures are made; the
 fixtures themselves are committed and the tests never read the reference.
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
 """
 from __future__ import annotations
 
@@ -77,7 +77,7 @@ def as_np(t):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="project root of hhkbble/sparton")
     args = ap.parse_args()
     for name, spec in CASES.items():
         dtype = spec[0]

@@ -8,11 +8,11 @@ with respect to the query / document representations as ``losses_<case>.npz``;
 they pin the loss oracle in ``oracle/losses_oracle.py`` before the tests trust
 it.
 
-This script needs the reference checkout (``--reference``, default
-``/root/reference``), which exists only where the fixtures are made; the
+This script needs a checkout of the reference (``--reference PATH``, the
+project root of hhkbble/sparton), which exists only where the fixtures are made; the
 fixtures themselves are committed and the tests never read the reference.
 
-    python tests/golden/make_golden_losses.py [--reference PATH]
+    python tests/golden/make_golden_losses.py --reference PATH
 """
 from __future__ import annotations
 
@@ -51,7 +51,7 @@ def make_reps(B, V, zero_frac, gen):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="project root of hhkbble/sparton")
     args = ap.parse_args(argv)
     ref = load_reference_train(args.reference)
     for name, (dtype, Bq, Bd, V, temp, zf, seed) in CASES.items():

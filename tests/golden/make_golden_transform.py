@@ -9,11 +9,11 @@ on the CPU under autograd, on seeded hidden states, masks and upstream
 gradients. Saves inputs, parameters, reps and every gradient as
 ``transform_<case>.npz``; they pin oracle/transform_oracle.py.
 
-This script needs the reference checkout (``--reference``, default
-``/root/reference``), which exists only where the fixtures are made; the
+This script needs a checkout of the reference (``--reference PATH``, the
+project root of hhkbble/sparton), which exists only where the fixtures are made; the
 fixtures themselves are committed and the tests never read the reference.
 
-    python tests/golden/make_golden_transform.py [--reference PATH]
+    python tests/golden/make_golden_transform.py --reference PATH
 """
 from __future__ import annotations
 
@@ -51,7 +51,7 @@ def build(model_type, D, V, seed):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="project root of hhkbble/sparton")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "training"))
     from model import ProjectionPyTorch, _get_backbone_and_head  # the reference's own
