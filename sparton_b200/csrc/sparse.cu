@@ -232,6 +232,13 @@ __global__ void __launch_bounds__(kTopkThreads)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int kStep = kTopkThreads * kTileU;
   if (threadIdx.x == 0) s_gt = 0;
+  // One CTA per row: a block barrier and this CTA's own shared memory.
+  auto csync = [&]() {
+    if (P > 1)
+      cluster.sync();
+    else
+      __syncthreads();
+  };
 
   // Radix select over the whole row: after the pass on bits [shift, shift+8),
   // `prefix` holds the top bits of K and `remaining` how many elements with
@@ -260,16 +267,20 @@ __global__ void __launch_bounds__(kTopkThreads)
         if (d < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
       }
     }
-    cluster.sync();  // every CTA's histogram is complete
+    csync();  // every CTA's histogram is complete
     // Digits in descending order, one per thread: the digit whose bucket
     // holds the remaining-th largest key of the prefix group.
     const int t = static_cast<int>(threadIdx.x);
     uint32_t own = 0, before = 0;
     if (t < 256) {
-      for (int r = 0; r < P; ++r) {
-        const uint32_t x = *cluster.map_shared_rank(hist + (255 - t), r);
-        own += x;
-        before += r < c ? x : 0u;
+      if (P == 1) {
+        own = hist[255 - t];
+      } else {
+        for (int r = 0; r < P; ++r) {
+          const uint32_t x = *cluster.map_shared_rank(hist + (255 - t), r);
+          own += x;
+          before += r < c ? x : 0u;
+        }
       }
     }
     int total;
@@ -279,7 +290,7 @@ __global__ void __launch_bounds__(kTopkThreads)
       s_remaining = remaining - above;
       s_eq_before = before;  // after the last pass: equals of K in the CTAs before this one
     }
-    cluster.sync();  // no CTA reads another's histogram past this point
+    csync();  // no CTA reads another's histogram past this point
     prefix = s_prefix;
     remaining = s_remaining;
     prefix_mask |= 0xFFu << shift;
@@ -290,9 +301,9 @@ __global__ void __launch_bounds__(kTopkThreads)
   // CTA 0's shared memory.
   const uint32_t K = prefix;
   const int n_gt = k - static_cast<int>(remaining);
-  uint32_t* dkey = cluster.map_shared_rank(skey, 0);
-  int32_t* did = cluster.map_shared_rank(sid, 0);
-  uint32_t* dgt = cluster.map_shared_rank(&s_gt, 0);
+  uint32_t* dkey = P > 1 ? cluster.map_shared_rank(skey, 0) : skey;
+  int32_t* did = P > 1 ? cluster.map_shared_rank(sid, 0) : sid;
+  uint32_t* dgt = P > 1 ? cluster.map_shared_rank(&s_gt, 0) : &s_gt;
   const unsigned lt = (1u << lane) - 1u;
   int eq_seen = static_cast<int>(s_eq_before);
   for (int base0 = v_lo; base0 < v_hi; base0 += kStep) {
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(kTopkThreads)
     }
     eq_seen += total;
   }
-  cluster.sync();  // CTA 0 holds all k candidates
+  csync();  // CTA 0 holds all k candidates
   if (c != 0) return;
   for (int i = k + static_cast<int>(threadIdx.x); i < k_pad; i += kTopkThreads) {
     skey[i] = 0;  // below every real key in the descending order
