@@ -592,6 +592,7 @@ def main(argv=None) -> int:
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     dt = _lib.DTYPE[c["dtype"]]
     chunks = row_chunks(B, S * D * torch.empty((), dtype=dh_dtype).element_size())
+    side = torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
     def step(k0=None, k1=None):
@@ -605,11 +606,20 @@ def main(argv=None) -> int:
         if k1 is not None:
             k1.record(stream)
         if world == 1:
+            # As the ops' backward does: the dH half on this stream, the dW / db
+            # half on a side stream, joined before the step ends.
+            side.wait_stream(stream)
             _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
                                        Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs,
-                                       dH.data_ptr(), dW.data_ptr(), _lib.ptr(db),
+                                       dH.data_ptr(), None, None,
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
-                       "bwd")
+                       "bwd dH")
+            _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
+                                       Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs,
+                                       None, dW.data_ptr(), _lib.ptr(db),
+                                       _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(),
+                                       side.cuda_stream), "bwd dW")
+            stream.wait_stream(side)
             return
         # Sharded, with SpartonHead's sharded backward schedule: partial dH in
         # chunks of batch rows, each chunk all-reduced (fp32, NCCL's stream)

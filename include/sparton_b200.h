@@ -167,7 +167,10 @@ size_t sparton_bwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V);
  *   the three outputs may be NULL to skip it.
  * Every output element is written (no pre-zeroing needed); the result is
  * deterministic (no atomics). Upstream accumulates with fp32 atomics into
- * zero-initialised fp32 buffers. */
+ * zero-initialised fp32 buffers.
+ * A call with only d_hidden and a call with only d_weight / d_bias may run
+ * concurrently on two streams with the same workspace (they write disjoint
+ * parts of it); running them so overlaps the two gathers. */
 int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx,
                 const void* hidden, const void* weight, int dtype,
                 int64_t B, int64_t S, int64_t D, int64_t V,
