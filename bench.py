@@ -10,12 +10,14 @@ quoted on): B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden
 U[32,256], upstream grad g ~ N(0,1); seeded synthetic data standing in for
 SPLADE batches. ``--workload`` selects the other BASELINE configurations
 (WORKLOADS below: config 3 V=250002, config 4 fp16 B=512 S=512, config 5
-D=4096 V=128256 without bias), same distributions as BASELINE.json states. With N GPUs the decoder is vocabulary-sharded over the ranks (the same
-total workload: strong scaling) and the partial d_hidden is all-reduced (fp32,
-NCCL).
+D=4096 V=128256 without bias), same distributions as BASELINE.json states.
+With N GPUs the decoder is vocabulary-sharded over the ranks (the same total
+workload: strong scaling) and the partial d_hidden is all-reduced (fp32, NCCL,
+in chunks of batch rows overlapping the backward; high-priority NCCL streams).
 
 One step = head forward (mask reduction + fused GEMM/max/argmax/log1p kernel)
-+ backward (sort by argmax, dH, dW, db) [+ all-reduce of dH].
++ backward (sort by argmax, dH, dW, db; single GPU: the dH and dW halves on two
+streams) [+ all-reduce of dH].
 
 Prints ONE JSON line on rank 0. ``value`` is the BASELINE metric, nominal
 fwd+bwd TFLOP/s = 4*B*S*D*V / step time, with inputs resident in HBM and the
@@ -28,6 +30,11 @@ pinned memory and a device->host read of reps inside the timed region.
 bf16 peak. ``cpu_baseline`` times the reference torch head (oracle/torch_head.py,
 a restatement of the reference's --head torch path) on the host cores on a
 bounded sample of the same workload.
+
+Further legs (``--legs``), reported as objects in the same line: ``losses``
+(InfoNCE and the fused regularisers on reps-shaped input), ``sparse`` (CSR and
+top-k of reps), ``transform`` (the MLM transform's kernels and SpartonProjection
+forward + backward).
 
 ``--impl reference`` times that CPU reference alone (rank 0; other ranks exit)
 and prints its line with ``"impl": "reference"``.
