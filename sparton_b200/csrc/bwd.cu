@@ -37,47 +37,18 @@
 #include <mutex>
 #include <type_traits>
 
+#include "dtype.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
 namespace sparton {
 namespace {
 
-template <typename T>
-__device__ __forceinline__ float ld_f(const T* p);
-template <>
-__device__ __forceinline__ float ld_f<float>(const float* p) {
-  return __ldg(p);
-}
-template <>
-__device__ __forceinline__ float ld_f<__half>(const __half* p) {
-  return __half2float(__ldg(p));
-}
-template <>
-__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat162float(__ldg(p));
-}
-
 // g' of one (b, v) entry; 0 when the head's output is 0 (max logit <= 0).
 template <typename T>
 __device__ __forceinline__ float scaled_grad(const T* g, const T* reps, size_t o) {
-  const float sc = ld_f<T>(reps + o);
-  return sc > 0.f ? ld_f<T>(g + o) * expf(-sc) : 0.f;
-}
-
-template <typename O>
-__device__ __forceinline__ O cvt_out(float x);
-template <>
-__device__ __forceinline__ float cvt_out<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) {
-  return __float2bfloat16_rn(x);
-}
-template <>
-__device__ __forceinline__ __half cvt_out<__half>(float x) {
-  return __float2half_rn(x);
+  const float sc = ldg_f32<T>(reps + o);
+  return sc > 0.f ? ldg_f32<T>(g + o) * expf(-sc) : 0.f;
 }
 
 // acc[i], acc[i+1] += c * f.x, c * f.y as one paired FMA (fma.rn.f32x2 on
@@ -211,7 +182,7 @@ __global__ void __launch_bounds__(1024)
     const int v = vb + lane;
     int key = -1;
     if (v < v_end) {
-      const float sc = ld_f<T>(reps + row + v);
+      const float sc = ldg_f32<T>(reps + row + v);
       const int s = __ldg(idx + row + v);
       if (sc > 0.f && s >= 0 && s < S) key = s;
     }
@@ -288,11 +259,11 @@ __global__ void __launch_bounds__(1024)
     int key = -1;
     float gp = 0.f;
     if (v < v_end) {
-      const float sc = ld_f<T>(reps + row + v);
+      const float sc = ldg_f32<T>(reps + row + v);
       const int s = __ldg(idx + row + v);
       if (sc > 0.f && s >= 0 && s < S) {
         key = s;
-        gp = ld_f<T>(g + row + v) * expf(-sc);
+        gp = ldg_f32<T>(g + row + v) * expf(-sc);
       }
     }
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
@@ -473,7 +444,7 @@ __device__ __forceinline__ void gather_row_full(const T* __restrict__ src, int B
   if (kMode == 1 && out_sum != nullptr) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xFFFFFFFFu, csum, o);
-    if (lane == 0) out_sum[r] = cvt_out<O>(csum);
+    if (lane == 0) out_sum[r] = from_f32<O>(csum);
   }
 }
 
@@ -543,7 +514,7 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
   if (kMode == 1 && out_sum != nullptr && d_lo == 0) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xFFFFFFFFu, csum, o);
-    if (lane == 0) out_sum[r] = cvt_out<O>(csum);
+    if (lane == 0) out_sum[r] = from_f32<O>(csum);
   }
 }
 
@@ -609,7 +580,7 @@ __global__ void __launch_bounds__(256) db_kernel(const T* __restrict__ g, const 
   if (v >= V) return;
   float acc = 0.f;
   for (int b = 0; b < B; ++b) acc += scaled_grad<T>(g, reps, static_cast<size_t>(b) * V + v);
-  db[v] = cvt_out<O>(acc);
+  db[v] = from_f32<O>(acc);
 }
 
 // ----------------------------------------------------------------------- host

@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "dtype.cuh"
 #include "internal.h"
 
 namespace sparton {
@@ -26,36 +27,6 @@ namespace {
 
 constexpr int kRegWarps = 8;  // rows are strided over the warps of a block
 constexpr int kTotalThreads = 1024;
-
-template <typename T>
-__device__ __forceinline__ float load_f(const T* p);
-template <>
-__device__ __forceinline__ float load_f<float>(const float* p) {
-  return __ldg(p);
-}
-template <>
-__device__ __forceinline__ float load_f<__half>(const __half* p) {
-  return __half2float(__ldg(p));
-}
-template <>
-__device__ __forceinline__ float load_f<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat162float(__ldg(p));
-}
-
-template <typename T>
-__device__ __forceinline__ T store_f(float x);
-template <>
-__device__ __forceinline__ float store_f<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ __half store_f<__half>(float x) {
-  return __float2half_rn(x);
-}
-template <>
-__device__ __forceinline__ __nv_bfloat16 store_f<__nv_bfloat16>(float x) {
-  return __float2bfloat16_rn(x);
-}
 
 // One block per 32 vocabulary columns (one per lane); warp w sums rows
 // b = w, w + 8, ... of its lane's column.
@@ -71,7 +42,7 @@ __global__ void __launch_bounds__(kRegWarps * 32)
   if (v < V) {
 #pragma unroll 8
     for (int b = warp; b < B; b += kRegWarps) {
-      const float x = load_f<T>(reps + static_cast<size_t>(b) * V + v);
+      const float x = ldg_f32<T>(reps + static_cast<size_t>(b) * V + v);
       col += x;
       ab += fabsf(x);
     }
@@ -145,9 +116,9 @@ __global__ void __launch_bounds__(256)
   const float cv = c1 * __ldg(colsum + v);
   for (int b = blockIdx.y; b < B; b += gridDim.y) {
     const size_t i = static_cast<size_t>(b) * V + v;
-    const float x = load_f<T>(reps + i);
+    const float x = ldg_f32<T>(reps + i);
     const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-    grad[i] = store_f<T>(fmaf(c0, s, cv));
+    grad[i] = from_f32<T>(fmaf(c0, s, cv));
   }
 }
 

@@ -27,6 +27,7 @@
 
 #include <cooperative_groups.h>
 
+#include "dtype.cuh"
 #include "internal.h"
 
 namespace sparton {
@@ -36,21 +37,6 @@ constexpr int kCsrChunk = 4096;
 constexpr int kCsrThreads = 256;
 constexpr int kTopkThreads = 512;
 constexpr int kTileU = 8;  // entries per lane per step of a row walk
-
-template <typename T>
-__device__ __forceinline__ float as_float(T x);
-template <>
-__device__ __forceinline__ float as_float<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ float as_float<__half>(__half x) {
-  return __half2float(x);
-}
-template <>
-__device__ __forceinline__ float as_float<__nv_bfloat16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
-}
 
 // Order-preserving unsigned key of an element (larger value -> larger key;
 // NaN above +inf, as torch.topk orders it) and its bit width.
@@ -131,7 +117,7 @@ __global__ void __launch_bounds__(kCsrThreads)
       x[u] = v < v1 ? row[v] : T{};
     }
 #pragma unroll
-    for (int u = 0; u < kTileU; ++u) n += (base + u * 32 + lane < v1 && as_float<T>(x[u]) > thr);
+    for (int u = 0; u < kTileU; ++u) n += (base + u * 32 + lane < v1 && to_f32<T>(x[u]) > thr);
   }
   n = block_sum(n, tmp);
   if (threadIdx.x == 0) chunk_cnt[static_cast<size_t>(b) * nchunks + ch] = n;
@@ -182,7 +168,7 @@ __global__ void __launch_bounds__(kCsrThreads)
 #pragma unroll
     for (int u = 0; u < kTileU; ++u) {
       const int v = base + u * 32 + lane;
-      keep[u] = __ballot_sync(0xFFFFFFFFu, v < v1 && as_float<T>(x[u]) > thr);
+      keep[u] = __ballot_sync(0xFFFFFFFFu, v < v1 && to_f32<T>(x[u]) > thr);
       warp_n += __popc(keep[u]);
     }
     // Columns before this warp's span in the step, then earlier u, then lower lanes.

@@ -27,6 +27,7 @@
 
 #include <type_traits>
 
+#include "dtype.cuh"
 #include "internal.h"
 
 namespace sparton {
@@ -37,39 +38,10 @@ constexpr int kColRows = 256;  // rows per CTA of the column kernel
 constexpr int kMaxPerLane = 32;  // D <= 1024 keeps a row in registers
 constexpr int kVecPerLane = 4;   // 8-column chunks per lane: D <= 1024, D % 8 == 0
 
-template <typename T>
-__device__ __forceinline__ float to_f(T x);
-template <>
-__device__ __forceinline__ float to_f<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ float to_f<__half>(__half x) {
-  return __half2float(x);
-}
-template <>
-__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
-}
-template <typename T>
-__device__ __forceinline__ T from_f(float x);
-template <>
-__device__ __forceinline__ float from_f<float>(float x) {
-  return x;
-}
-template <>
-__device__ __forceinline__ __half from_f<__half>(float x) {
-  return __float2half_rn(x);
-}
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) {
-  return __float2bfloat16_rn(x);
-}
-
 // gelu(y) = y * Phi(y), rounded to T as a separate activation module would.
 template <typename T>
 __device__ __forceinline__ float gelu_t(float y) {
-  return to_f<T>(from_f<T>(0.5f * y * (1.f + erff(y * 0.70710678118654752f))));
+  return to_f32<T>(from_f32<T>(0.5f * y * (1.f + erff(y * 0.70710678118654752f))));
 }
 // d gelu / dy = Phi(y) + y * phi(y).
 __device__ __forceinline__ float gelu_grad(float y) {
@@ -89,7 +61,7 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
     const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = to_f<T>(e[i]);
+    for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
   }
 }
 template <typename T>
@@ -101,7 +73,7 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
     uint4 u;
     T* e = reinterpret_cast<T*>(&u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = from_f<T>(v[i]);
+    for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(v[i]);
     *reinterpret_cast<uint4*>(p) = u;
   }
 }
@@ -169,7 +141,7 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
       const int d = lane + 32 * i;
-      g[i] = d < D ? gelu_t<T>(to_f<T>(yr[d])) : 0.f;
+      g[i] = d < D ? gelu_t<T>(to_f32<T>(yr[d])) : 0.f;
       s += g[i];
     }
     mean = warp_sum(s) * inv_d;
@@ -185,21 +157,21 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     for (int i = 0; i < kMaxPerLane; ++i) {
       const int d = lane + 32 * i;
       if (d < D)
-        hr[d] = from_f<T>((g[i] - mean) * rstd * to_f<T>(gamma[d]) + to_f<T>(beta[d]));
+        hr[d] = from_f32<T>((g[i] - mean) * rstd * to_f32<T>(gamma[d]) + to_f32<T>(beta[d]));
     }
   } else {  // long rows: recompute gelu in each pass
     float s = 0.f;
-    for (int d = lane; d < D; d += 32) s += gelu_t<T>(to_f<T>(yr[d]));
+    for (int d = lane; d < D; d += 32) s += gelu_t<T>(to_f32<T>(yr[d]));
     mean = warp_sum(s) * inv_d;
     float q = 0.f;
     for (int d = lane; d < D; d += 32) {
-      const float c = gelu_t<T>(to_f<T>(yr[d])) - mean;
+      const float c = gelu_t<T>(to_f32<T>(yr[d])) - mean;
       q += c * c;
     }
     rstd = rsqrtf(warp_sum(q) * inv_d + eps);
     for (int d = lane; d < D; d += 32)
-      hr[d] = from_f<T>((gelu_t<T>(to_f<T>(yr[d])) - mean) * rstd * to_f<T>(gamma[d]) +
-                        to_f<T>(beta[d]));
+      hr[d] = from_f32<T>((gelu_t<T>(to_f32<T>(yr[d])) - mean) * rstd * to_f32<T>(gamma[d]) +
+                        to_f32<T>(beta[d]));
   }
   if (lane == 0) {
     mean_out[r] = mean;
@@ -264,20 +236,20 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   // mean(dxh) and mean(dxh * xh) over the row
   float a = 0.f, b = 0.f;
   for (int d = lane; d < D; d += 32) {
-    const float yv = to_f<T>(y[o + d]);
+    const float yv = to_f32<T>(y[o + d]);
     const float xh = (gelu_t<T>(yv) - mu) * rs;
-    const float dxh = to_f<T>(dh[o + d]) * to_f<T>(gamma[d]);
+    const float dxh = to_f32<T>(dh[o + d]) * to_f32<T>(gamma[d]);
     a += dxh;
     b += dxh * xh;
   }
   a = warp_sum(a) * inv_d;
   b = warp_sum(b) * inv_d;
   for (int d = lane; d < D; d += 32) {
-    const float yv = to_f<T>(y[o + d]);
+    const float yv = to_f32<T>(y[o + d]);
     const float xh = (gelu_t<T>(yv) - mu) * rs;
-    const float dxh = to_f<T>(dh[o + d]) * to_f<T>(gamma[d]);
+    const float dxh = to_f32<T>(dh[o + d]) * to_f32<T>(gamma[d]);
     const float dg = rs * (dxh - a - xh * b);
-    dy[o + d] = from_f<T>(dg * gelu_grad(yv));
+    dy[o + d] = from_f32<T>(dg * gelu_grad(yv));
   }
   }
 }
@@ -298,11 +270,11 @@ __global__ void __launch_bounds__(256)
   if (col < D) {
     for (int r = r0 + warp; r < r1; r += 8) {
       const size_t o = static_cast<size_t>(r) * D + col;
-      const float g = to_f<T>(dh[o]);
-      const float xh = (gelu_t<T>(to_f<T>(y[o])) - mean[r]) * rstd[r];
+      const float g = to_f32<T>(dh[o]);
+      const float xh = (gelu_t<T>(to_f32<T>(y[o])) - mean[r]) * rstd[r];
       pg += g * xh;
       pb += g;
-      pd += to_f<T>(dy[o]);
+      pd += to_f32<T>(dy[o]);
     }
   }
   s[0][warp][lane] = pg;
@@ -380,9 +352,9 @@ __global__ void __launch_bounds__(256)
     b += partials[(static_cast<size_t>(i) * 3 + 1) * D + col];
     c += partials[(static_cast<size_t>(i) * 3 + 2) * D + col];
   }
-  if (d_gamma != nullptr) d_gamma[col] = from_f<T>(g);
-  if (d_beta != nullptr) d_beta[col] = from_f<T>(b);
-  if (d_bias != nullptr) d_bias[col] = from_f<T>(c);
+  if (d_gamma != nullptr) d_gamma[col] = from_f32<T>(g);
+  if (d_beta != nullptr) d_beta[col] = from_f32<T>(b);
+  if (d_bias != nullptr) d_bias[col] = from_f32<T>(c);
 }
 
 bool vec_path(int D) { return D % 8 == 0 && D <= 8 * 32 * kVecPerLane; }
