@@ -679,6 +679,12 @@ def main(argv=None) -> int:
     step_ms = max_over_ranks(sum(a.elapsed_time(e) for a, e in step_ev) / args.steps)
     kern_ms = sum(a.elapsed_time(e) for a, e in kern_ev) / args.steps
     kern_ms_max = max_over_ranks(kern_ms)
+    # forward part (mask + pack prepare + forward kernel) and backward part
+    # (sort, gathers [, all-reduce]) of the same timed steps
+    fwd_part_ms = max_over_ranks(
+        sum(step_ev[i][0].elapsed_time(kern_ev[i][1]) for i in range(args.steps)) / args.steps)
+    bwd_part_ms = max_over_ranks(
+        sum(kern_ev[i][1].elapsed_time(step_ev[i][1]) for i in range(args.steps)) / args.steps)
     # mask_prepare + pack_prepare + forward; backward: sort, dH gather, dW list,
     # dW gather (db, when there is a bias, is summed inside the dW gather);
     # sharded, a sort and a dH gather per chunk of batch rows.
@@ -731,6 +737,8 @@ def main(argv=None) -> int:
         "algorithmic_tflops": round((2.0 * D * V * T + 4.0 * D * B * V) / (step_ms * 1e-3) / 1e12, 2),
         "frac_of_bf16_peak_nominal": round(value / peak, 4),
         "fwd_kernel_ms": round(kern_ms_max, 4),
+        "fwd_ms": round(fwd_part_ms, 4),
+        "bwd_ms": round(bwd_part_ms, 4),
         "roofline": {"kernel": "fwd_tc_kernel", "bound": "tensor", "achieved": round(achieved, 2),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "frac_of_sustained": round(achieved / float(peaks["bf16_tflops_sustained"]), 4),
