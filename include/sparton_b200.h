@@ -252,7 +252,8 @@ size_t sparton_transform_workspace_size(int64_t rows, int64_t D);
  * dy [rows, D] = d(gelu + LayerNorm)/dy (the caller's BLAS then forms
  * dx = dy @ Wd and dWd = dy^T @ x), and, each optional (NULL skips it),
  * d_gamma, d_beta [D] and d_bias [D] = sum over rows of dy (the dense bias),
- * in `dtype`, summed in a fixed order. */
+ * in `dtype`, summed in a fixed order (rows <= 65535 * 256 when any of them
+ * is requested). */
 int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, const float* mean,
                           const float* rstd, int dtype, int64_t rows, int64_t D, void* dy,
                           void* d_gamma, void* d_beta, void* d_bias, void* workspace,

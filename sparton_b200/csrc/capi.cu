@@ -346,6 +346,10 @@ int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, cons
     return fail(SPARTON_ERR_UNSUPPORTED, "sizes out of range (rows=%lld D=%lld)",
                 (long long)rows, (long long)D);
   const bool cols = d_gamma != nullptr || d_beta != nullptr || d_bias != nullptr;
+  // the column sums take one CTA row per 256 rows, 65535 at most
+  if (cols && rows > 65535ll * 256)
+    return fail(SPARTON_ERR_UNSUPPORTED, "rows=%lld above %lld for the parameter gradients",
+                (long long)rows, 65535ll * 256);
   if (cols) SPARTON_TRY(check_workspace(workspace, workspace_size, transform_workspace_bytes(rows, D)));
   if (rows == 0) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
