@@ -149,7 +149,7 @@ template <typename T>
 __global__ void __launch_bounds__(1024)
     bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
                     const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
-                    int* __restrict__ perm, float* __restrict__ gperm, unsigned int* status,
+                    int2* __restrict__ ent, unsigned int* status,
                     unsigned int* row_counter) {
   extern __shared__ int cnt[];  // [nw][S], then tot[S] and, when P > 1, base[S], full[S]
   __shared__ int scan_tmp[33];
@@ -251,8 +251,7 @@ __global__ void __launch_bounds__(1024)
   if (c == 0 && threadIdx.x == 0) orow[S] = scan_tmp[32];
   __syncthreads();
 
-  int* prow = perm + row;
-  float* grow = gperm + row;
+  int2* erow = ent + row;
   const unsigned lt = (1u << lane) - 1u;
   for (int vb = v_begin; vb < v_end; vb += 32) {
     const int v = vb + lane;
@@ -271,22 +270,21 @@ __global__ void __launch_bounds__(1024)
     if (key >= 0) slot = my[key] + __popc(peers & lt);
     __syncwarp();
     if (key >= 0) {
-      prow[slot] = v;
-      grow[slot] = gp;
+      erow[slot] = make_int2(v, __float_as_int(gp));
       if (lane == __ffs(peers) - 1) my[key] += __popc(peers);
     }
     __syncwarp();
   }
 }
 
-// Vocab-major list for dW: wrow[v*B + b] = b*S + idx[b,v] and wcoef[v*B + b] =
-// g'[b,v] (0, with a harmless valid row, when the head's output is 0). Tiles of
+// Vocab-major list for dW: went[v*B + b] = (b*S + idx[b,v], bits of g'[b,v])
+// (g' = 0, with a harmless valid row, when the head's output is 0). Tiles of
 // 32 batch rows x 32 vocab ids through shared memory: both sides coalesced.
 template <typename T>
 __global__ void __launch_bounds__(256)
     dw_list_kernel(const T* __restrict__ g, const T* __restrict__ reps,
-                   const int32_t* __restrict__ idx, int B, int S, int V, int* __restrict__ wrow,
-                   float* __restrict__ wcoef, unsigned int* status) {
+                   const int32_t* __restrict__ idx, int B, int S, int V, int2* __restrict__ went,
+                   unsigned int* status) {
   __shared__ float cs[32][33];
   __shared__ int rs[32][33];
   const int v0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
@@ -310,8 +308,7 @@ __global__ void __launch_bounds__(256)
     const int v = v0 + i, b = b0 + tx;
     if (v < V && b < B) {
       const size_t o = static_cast<size_t>(v) * B + b;
-      wrow[o] = rs[tx][i];
-      wcoef[o] = cs[tx][i];
+      went[o] = make_int2(rs[tx][i], __float_as_int(cs[tx][i]));
     }
   }
 }
@@ -387,8 +384,7 @@ __device__ __forceinline__ void entry_range(int q, int B, int S, int V, const in
 template <typename T, typename O, int NC, int kMode>
 __device__ __forceinline__ void gather_row_full(const T* __restrict__ src, int B, int S, int D,
                                                 int V, const int* __restrict__ offs,
-                                                const int* __restrict__ ent_row,
-                                                const float* __restrict__ ent_coef, int q,
+                                                const int2* __restrict__ ent, int q,
                                                 O* __restrict__ out, O* __restrict__ out_sum,
                                                 int lane) {
   int r, e0, e1;
@@ -406,8 +402,9 @@ __device__ __forceinline__ void gather_row_full(const T* __restrict__ src, int B
       int my_row = 0;
       float my_coef = 0.f;
       if (lane < n) {
-        my_row = __ldg(ent_row + eb + lane);
-        my_coef = __ldg(ent_coef + eb + lane);
+        const int2 e = __ldg(ent + eb + lane);
+        my_row = e.x;
+        my_coef = __int_as_float(e.y);
       }
       if (kMode == 1 && d0 == 0) csum += my_coef;
       for (int j = 0; j < n; j += kGUnroll) {
@@ -452,8 +449,7 @@ __device__ __forceinline__ void gather_row_full(const T* __restrict__ src, int B
 template <typename T, typename O, int G, int U, int kMode>
 __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int B, int S, int D,
                                                  int V, const int* __restrict__ offs,
-                                                 const int* __restrict__ ent_row,
-                                                 const float* __restrict__ ent_coef, int q,
+                                                 const int2* __restrict__ ent, int q,
                                                  int d_lo, int width, O* __restrict__ out,
                                                  O* __restrict__ out_sum, int lane) {
   static_assert(G == 1 || G == 2 || G == 4, "lane groups");
@@ -472,8 +468,9 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
   int nx_row = 0;
   float nx_coef = 0.f;
   if (lane < e1 - e0) {
-    nx_row = ld_list(ent_row + e0 + lane);
-    nx_coef = ld_list(ent_coef + e0 + lane);
+    const int2 e = ld_list(ent + e0 + lane);
+    nx_row = e.x;
+    nx_coef = __int_as_float(e.y);
   }
   for (int eb = e0; eb < e1; eb += 32) {
     const int n = min(32, e1 - eb);
@@ -482,8 +479,9 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
     nx_row = 0;
     nx_coef = 0.f;
     if (lane < e1 - eb - 32) {  // the next batch, while this one is gathered
-      nx_row = ld_list(ent_row + eb + 32 + lane);
-      nx_coef = ld_list(ent_coef + eb + 32 + lane);
+      const int2 e = ld_list(ent + eb + 32 + lane);
+      nx_row = e.x;
+      nx_coef = __int_as_float(e.y);
     }
     if (kMode == 1) csum += my_coef;
     for (int j = 0; j < n; j += U * G) {
@@ -525,7 +523,7 @@ __device__ __forceinline__ void gather_row_slice(const T* __restrict__ src, int 
 template <typename T, typename O, int NC, int G, int U, int kMode>
 __global__ void __launch_bounds__(kGWarps * 32, 4)
     gather_kernel(const T* __restrict__ src, int B, int S, int D, int V, const int* __restrict__ offs,
-                  const int* __restrict__ ent_row, const float* __restrict__ ent_coef, int n_rows,
+                  const int2* __restrict__ ent, int n_rows,
                   int slice_w, int n_slices, O* __restrict__ out, O* __restrict__ out_sum,
                   unsigned int* row_counter) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -543,12 +541,12 @@ __global__ void __launch_bounds__(kGWarps * 32, 4)
       int qn = 0;
       if (lane == 0) qn = static_cast<int>(atomicAdd(row_counter, 1u));
       if constexpr (G == 0) {
-        gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, q, out,
+        gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent, q, out,
                                          out_sum, lane);
       } else {
         const int sl = q / n_rows;
         const int d_lo = sl * slice_w;
-        gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+        gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent,
                                             q - sl * n_rows, d_lo, min(slice_w, D - d_lo), out,
                                             out_sum, lane);
       }
@@ -558,7 +556,7 @@ __global__ void __launch_bounds__(kGWarps * 32, 4)
     // dW: one row per warp.
     const int r = blockIdx.x * kGWarps + warp;
     if (r < n_rows)
-      gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, out, out_sum,
+      gather_row_full<T, O, NC, kMode>(src, B, S, D, V, offs, ent, r, out, out_sum,
                                        lane);
   } else {
     // dW: one (slice, row) per warp; blocks are slice-major (the block scheduler
@@ -568,7 +566,7 @@ __global__ void __launch_bounds__(kGWarps * 32, 4)
     const int r = (blockIdx.x - sl * per_slice) * kGWarps + warp;
     const int d_lo = sl * slice_w;
     if (r < n_rows)
-      gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, r, d_lo,
+      gather_row_slice<T, O, G, U, kMode>(src, B, S, D, V, offs, ent, r, d_lo,
                                           min(slice_w, D - d_lo), out, out_sum, lane);
   }
 }
@@ -640,8 +638,8 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
     }
   }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, bwd_sort_kernel<T>, static_cast<const T*>(grad_reps),
-                                           static_cast<const T*>(reps), idx, S, V, ws.offs, ws.perm,
-                                           ws.gperm, ws.status, ws.row_counter);
+                                           static_cast<const T*>(reps), idx, S, V, ws.offs, ws.ent,
+                                           ws.status, ws.row_counter);
   if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
   return SPARTON_OK;
 }
@@ -650,8 +648,7 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
 // resident CTAs per SM (occupancy API, cached per device) x SMs, capped by the
 // work; for dW one CTA per kGWarps rows of each slice.
 template <typename T, typename O, int NC, int G, int U, int kMode>
-int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, const int* ent_row,
-                     const float* ent_coef, int n_rows, O* out, O* out_sum,
+int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, const int2* ent, int n_rows, O* out, O* out_sum,
                      unsigned int* row_counter, cudaStream_t stream) {
   static std::mutex mu;
   static int per_sm[64] = {};
@@ -681,7 +678,7 @@ int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, 
   const long long cap = kMode == 0 ? static_cast<long long>(bps) * device_sm_count() : need;
   const unsigned grid = static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
   gather_kernel<T, O, NC, G, U, kMode><<<grid, block, 0, stream>>>(
-      src, B, S, D, V, offs, ent_row, ent_coef, n_rows, slice_w, n_slices, out, out_sum,
+      src, B, S, D, V, offs, ent, n_rows, slice_w, n_slices, out, out_sum,
       row_counter);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gather_kernel launch");
@@ -693,28 +690,28 @@ int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, 
 // (64 at the least).
 template <typename T, typename O, int kMode>
 int launch_gather(const T* src, long long col_bytes, int B, int S, int D, int V, const int* offs,
-                  const int* ent_row, const float* ent_coef, int n_rows, O* out, O* out_sum,
+                  const int2* ent, int n_rows, O* out, O* out_sum,
                   unsigned int* row_counter, cudaStream_t stream) {
   if (col_bytes * D > kGatherL2Budget && D > 64) {
     if (D > 256 && col_bytes * 256 <= kGatherL2Budget)
-      return launch_gather_nc<T, O, 1, 1, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+      return launch_gather_nc<T, O, 1, 1, 4, kMode>(src, B, S, D, V, offs, ent,
                                                     n_rows, out, out_sum, row_counter, stream);
     if (D > 128 && col_bytes * 128 <= kGatherL2Budget)
-      return launch_gather_nc<T, O, 1, 2, 4, kMode>(src, B, S, D, V, offs, ent_row, ent_coef,
+      return launch_gather_nc<T, O, 1, 2, 4, kMode>(src, B, S, D, V, offs, ent,
                                                     n_rows, out, out_sum, row_counter, stream);
-    return launch_gather_nc<T, O, 1, 4, 8, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+    return launch_gather_nc<T, O, 1, 4, 8, kMode>(src, B, S, D, V, offs, ent, n_rows,
                                                   out, out_sum, row_counter, stream);
   }
   if (D <= 256)
-    return launch_gather_nc<T, O, 1, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+    return launch_gather_nc<T, O, 1, 0, 0, kMode>(src, B, S, D, V, offs, ent, n_rows,
                                                   out, out_sum, row_counter, stream);
   if (D <= 512)
-    return launch_gather_nc<T, O, 2, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+    return launch_gather_nc<T, O, 2, 0, 0, kMode>(src, B, S, D, V, offs, ent, n_rows,
                                                   out, out_sum, row_counter, stream);
   if (D <= 768)
-    return launch_gather_nc<T, O, 3, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+    return launch_gather_nc<T, O, 3, 0, 0, kMode>(src, B, S, D, V, offs, ent, n_rows,
                                                   out, out_sum, row_counter, stream);
-  return launch_gather_nc<T, O, 4, 0, 0, kMode>(src, B, S, D, V, offs, ent_row, ent_coef, n_rows,
+  return launch_gather_nc<T, O, 4, 0, 0, kMode>(src, B, S, D, V, offs, ent, n_rows,
                                                 out, out_sum, row_counter, stream);
 }
 
@@ -723,8 +720,7 @@ int launch_dh(const void* weight, int B, int S, int D, int V, void* d_hidden,
               const BwdWorkspace& ws, cudaStream_t stream) {
   // dH gathers rows of W in random order: its working set is all of W.
   return launch_gather<T, O, 0>(static_cast<const T*>(weight),
-                                static_cast<long long>(V) * sizeof(T), B, S, D, V, ws.offs, ws.perm,
-                                ws.gperm, B * S, static_cast<O*>(d_hidden), nullptr,
+                                static_cast<long long>(V) * sizeof(T), B, S, D, V, ws.offs, ws.ent, B * S, static_cast<O*>(d_hidden), nullptr,
                                 ws.row_counter, stream);
 }
 
@@ -734,16 +730,15 @@ int launch_dw(const void* grad_reps, const void* reps, const int32_t* idx, const
               cudaStream_t stream) {
   const dim3 lgrid(static_cast<unsigned>((V + 31) / 32), static_cast<unsigned>((B + 31) / 32));
   dw_list_kernel<T><<<lgrid, 256, 0, stream>>>(static_cast<const T*>(grad_reps),
-                                               static_cast<const T*>(reps), idx, B, S, V, ws.wrow,
-                                               ws.wcoef, ws.status);
+                                               static_cast<const T*>(reps), idx, B, S, V, ws.went,
+                                               ws.status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dw_list_kernel launch");
   // dW warps walk the batch rows in step: the working set is the H[b] of the
   // ~kDwRowsInFlight batch rows they span.
   return launch_gather<T, O, 1>(static_cast<const T*>(hidden),
                                 static_cast<long long>(kDwRowsInFlight) * S * sizeof(T), B, S, D, V,
-                                nullptr, ws.wrow,
-                                ws.wcoef, V, static_cast<O*>(d_weight), static_cast<O*>(d_bias),
+                                nullptr, ws.went, V, static_cast<O*>(d_weight), static_cast<O*>(d_bias),
                                 nullptr, stream);
 }
 

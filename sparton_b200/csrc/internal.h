@@ -113,15 +113,13 @@ struct BwdWorkspace {
   unsigned int* status;
   unsigned int* row_counter;
   int* offs;
-  int* perm;
-  float* gperm;
-  int* wrow;
-  float* wcoef;
+  int2* ent;   // [B][V] (v, bits of g') in CSR order by argmax position
+  int2* went;  // [V][B] (b*S + idx[b,v], bits of g'), vocab-major
 };
 
 inline size_t bwd_workspace_bytes(int64_t B, int64_t S, int64_t V) {
   return 256 + align256(static_cast<size_t>(B * (S + 1)) * 4) +
-         4 * align256(static_cast<size_t>(B * V) * 4);
+         2 * align256(static_cast<size_t>(B * V) * 8);
 }
 
 inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t V) {
@@ -132,13 +130,9 @@ inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t 
   size_t off = 256;
   w.offs = reinterpret_cast<int*>(base + off);
   off += align256(static_cast<size_t>(B * (S + 1)) * 4);
-  w.perm = reinterpret_cast<int*>(base + off);
-  off += align256(static_cast<size_t>(B * V) * 4);
-  w.gperm = reinterpret_cast<float*>(base + off);
-  off += align256(static_cast<size_t>(B * V) * 4);
-  w.wrow = reinterpret_cast<int*>(base + off);
-  off += align256(static_cast<size_t>(B * V) * 4);
-  w.wcoef = reinterpret_cast<float*>(base + off);
+  w.ent = reinterpret_cast<int2*>(base + off);
+  off += align256(static_cast<size_t>(B * V) * 8);
+  w.went = reinterpret_cast<int2*>(base + off);
   return w;
 }
 
