@@ -45,7 +45,7 @@ def test_workspace_sizes(lib):
     fw = lib.sparton_fwd_workspace_size(B, S, D, V)
     assert fw >= 256 + 4 * B + 4 * B * (S // 32)
     bw = lib.sparton_bwd_workspace_size(B, S, D, V)
-    assert bw >= 4 * B * (S + 1) + 8 * B * V
+    assert bw >= 256 + 4 * B * (S + 1) + 2 * 8 * B * V  # offsets + two 8-byte record lists
     assert lib.sparton_fwd_workspace_size(-1, S, D, V) == 0
 
 
@@ -100,3 +100,35 @@ def test_check_raises_python_errors():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ERR_CUDA, "x")
     _lib.check(_lib.OK, "x")
+
+
+def test_components_validate_before_any_launch(lib):
+    """Argument checks of the entry points around the head run on the host,
+    before any device access, so they answer without a GPU."""
+    d = ctypes.c_void_p(0x1000)
+    ws = ctypes.c_void_p(0x100000)
+    # top-k: k outside [0, V], or above the 4096 the kernel sorts in shared memory
+    assert lib.sparton_reps_topk(d, 2, 4, 100, 101, d, d, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_reps_topk(d, 2, 4, 10000, 4097, d, d, None) == _lib.ERR_UNSUPPORTED
+    assert lib.sparton_reps_topk(d, 9, 4, 100, 5, d, d, None) == _lib.ERR_UNSUPPORTED  # dtype
+    # CSR: no row pointers, negative capacity, capacity without outputs, small workspace
+    wsz = lib.sparton_sparse_workspace_size(4, 100)
+    assert lib.sparton_reps_csr(d, 2, 4, 100, 0.0, None, None, None, 0, ws, wsz, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_reps_csr(d, 2, 4, 100, 0.0, d, None, None, -1, ws, wsz, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_reps_csr(d, 2, 4, 100, 0.0, d, None, None, 10, ws, wsz, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_reps_csr(d, 2, 4, 100, 0.0, d, None, None, 0, ws, 4, None) == \
+        _lib.ERR_WORKSPACE
+    # transform: missing pointers, negative eps, too many rows for the parameter sums
+    assert lib.sparton_transform_fwd(d, d, None, 1e-5, 2, 8, 16, d, d, d, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_transform_fwd(d, d, d, -1.0, 2, 8, 16, d, d, d, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    rows = 65535 * 256 + 1
+    assert lib.sparton_transform_bwd(d, d, d, d, d, 2, rows, 16, d, d, None, None, ws,
+                                     lib.sparton_transform_workspace_size(rows, 16), None) == \
+        _lib.ERR_UNSUPPORTED
+    # regularisers: small workspace
+    assert lib.sparton_reg_fwd(d, 2, 4, 100, 1.0, 1.0, d, d, ws, 1, None) == _lib.ERR_WORKSPACE
