@@ -343,20 +343,10 @@ constexpr int kGUnroll = 4;
 // Sliced gathers: the entry lists are read once per slice and the outputs
 // written once, so both go through L2 evict-first (ld/st .cs) and leave it to
 // the slice of src, which is gathered many times.
-#ifndef SPARTON_SLICE_STREAM_LISTS
-#define SPARTON_SLICE_STREAM_LISTS 1
-#endif
-#ifndef SPARTON_SLICE_STREAM_STORES
-#define SPARTON_SLICE_STREAM_STORES 1
-#endif
-constexpr bool kSliceStreamStores = SPARTON_SLICE_STREAM_STORES != 0;
+constexpr bool kSliceStreamStores = true;
 template <typename X>
 __device__ __forceinline__ X ld_list(const X* p) {
-#if SPARTON_SLICE_STREAM_LISTS
   return __ldcs(p);
-#else
-  return __ldg(p);
-#endif
 }
 // Bytes of gathered data that are expected to stay resident in the 126 MB L2
 // next to the other traffic of the kernel, and the batch rows that the dW
