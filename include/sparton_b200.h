@@ -85,6 +85,7 @@ typedef enum {
 #define SPARTON_DEV_TIMEOUT_MMA 0x102u
 #define SPARTON_DEV_TIMEOUT_EPILOGUE 0x103u
 #define SPARTON_DEV_TIMEOUT_DRAIN 0x104u
+#define SPARTON_DEV_TIMEOUT_SELFTEST 0x1F0u /* sparton_selftest_wait_timeout only */
 
 int sparton_abi_version(void);
 
@@ -102,6 +103,11 @@ size_t sparton_fwd_workspace_size(int64_t B, int64_t S, int64_t D, int64_t V);
  *   hidden [B,S,D], weight [V,D], bias [V] (NULL = no bias), all `dtype`
  *   mask   [B,S] of `mask_dtype`
  *   reps   [B,V] `dtype` (out), idx [B,V] int32 (out; upstream uses int64)
+ * idx may be NULL: the inference forward, which keeps the max alone and
+ * stores reps only. It replaces upstream's no-argmax forward fused_sparton_fwd
+ * (sparton_kernel.py:372-394, reduce kernel :257-334), whose consumer is an
+ * encode under no_grad (training/model.py:141-144); reps are identical to
+ * those of the call with idx.
  * bf16 / f16 run on tcgen05 tensor cores with fp32 accumulation; f32 runs an
  * exact fp32 FMA path. Launches sparton_mask_prepare + sparton_fwd_prepared. */
 int sparton_fwd(const void* hidden, const void* weight, const void* bias,
@@ -145,13 +151,25 @@ int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bia
  *  - every call on a device shares the one array: calls that overlap on the
  *    GPU (e.g. on two streams without ordering between them) race and corrupt
  *    each other; serialise them;
- *  - the first call on each device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture begins. */
+ *  - every call looks up the array's device address (cudaGetSymbolAddress)
+ *    with the calling device current; the address is not cached, so it stays
+ *    right after a cudaDeviceReset, which reloads the module and may move the
+ *    array. The first call on a device loads the module there: make it before
+ *    any stream capture begins;
+ *  - a kernel that gave up on a bounded device wait leaves partial reps / idx
+ *    and records a nonzero code in the array's status word, which only
+ *    sparton_fwd_noalloc_status can read. */
 int sparton_fwd_noalloc(const void* hidden, const void* weight, const void* bias,
                         const void* mask, int mask_dtype, int dtype,
                         int64_t B, int64_t S, int64_t D, int64_t V,
                         void* reps, int32_t* idx, void* stream);
+
+/* Device status word (SPARTON_DEV_*) that the last sparton_fwd_noalloc call on
+ * the current device left in the library's scratch array; synchronises
+ * `stream` (pass the stream of that call). 0 = no device-side timeout. The
+ * counterpart of sparton_read_device_status for the allocation-free forward,
+ * whose scratch the caller has no pointer to. */
+int sparton_fwd_noalloc_status(void* stream, uint32_t* code);
 
 /* --------------------------------------------------------------- backward */
 
@@ -264,6 +282,19 @@ int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, cons
 /* Copies the device status word of a workspace used by sparton_fwd /
  * sparton_bwd to *code (synchronises `stream`). 0 = no device-side timeout. */
 int sparton_read_device_status(const void* workspace, void* stream, uint32_t* code);
+
+/* Self-test of the bounded device waits; no counterpart in the reference (its
+ * kernels never wait on one another). Launches one small kernel whose waits
+ * nobody completes, through the same bounded-wait routine the forward uses:
+ * one wait gives up after `limit_us` microseconds (1 .. 1e6) and records
+ * SPARTON_DEV_TIMEOUT_SELFTEST in word 0 of `workspace` (>= 256 bytes, 256-byte
+ * aligned); a second wait, with the production limit, leaves early through the
+ * abort flag the first one raised. Word 1 = microseconds the first wait
+ * waited, word 2 = 1 when the second left through the abort flag. Nothing
+ * faults and the kernel ends by itself; the context stays usable. Read the
+ * words (or sparton_read_device_status) after the stream has run it. */
+int sparton_selftest_wait_timeout(uint32_t limit_us, void* workspace, size_t workspace_size,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

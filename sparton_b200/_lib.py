@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "sparton_mask_prepare",
     "sparton_fwd_prepared",
     "sparton_fwd_noalloc",
+    "sparton_fwd_noalloc_status",
     "sparton_bwd_workspace_size",
     "sparton_bwd",
     "sparton_reg_workspace_size",
@@ -50,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "sparton_transform_workspace_size",
     "sparton_transform_bwd",
     "sparton_read_device_status",
+    "sparton_selftest_wait_timeout",
 )
 
 _lock = threading.Lock()
@@ -78,6 +80,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_fwd_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i64, _i64, _i64, _i64,
                                         _vp, _vp, _vp]
     lib.sparton_fwd_noalloc.restype = _i
+    lib.sparton_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint32)]
+    lib.sparton_fwd_noalloc_status.restype = _i
     lib.sparton_bwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64,
                                 _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]
     lib.sparton_bwd.restype = _i
@@ -103,6 +107,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_transform_bwd.restype = _i
     lib.sparton_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
     lib.sparton_read_device_status.restype = _i
+    lib.sparton_selftest_wait_timeout.argtypes = [ctypes.c_uint32, _vp, _sz, _vp]
+    lib.sparton_selftest_wait_timeout.restype = _i
 
 
 def load() -> ctypes.CDLL:

@@ -16,6 +16,7 @@ namespace {
 thread_local char g_last_error[512] = "";
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+}  // namespace
 
 int check_sizes(int64_t B, int64_t S, int64_t D, int64_t V) {
   if (B < 0 || S < 0 || D < 0 || V < 0)
@@ -46,6 +47,7 @@ int check_device() {
   return SPARTON_OK;
 }
 
+namespace {
 int check_workspace(const void* ws, size_t have, size_t need) {
   if (ws == nullptr || have < need)
     return fail(SPARTON_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given%s", need, have,
@@ -145,8 +147,7 @@ int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bia
   SPARTON_TRY(check_dtype(dtype));
   SPARTON_TRY(check_workspace(workspace, workspace_size, fwd_workspace_bytes(B, S)));
   if (B == 0 || V == 0) return SPARTON_OK;
-  if (reps == nullptr || idx == nullptr)
-    return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps / idx output is NULL");
+  if (reps == nullptr) return fail(SPARTON_ERR_INVALID_ARGUMENT, "reps output is NULL");
   if ((S > 0 && (hidden == nullptr || D == 0)) || weight == nullptr)
     return fail(SPARTON_ERR_INVALID_ARGUMENT, "hidden / weight is NULL or D == 0");
   if (!aligned(hidden, 16) || !aligned(weight, 16))
@@ -163,7 +164,8 @@ int sparton_fwd_prepared(const void* hidden, const void* weight, const void* bia
   if (S == 0) {
     // No positions at all: every output is the empty-row value (0, index 0).
     cudaError_t e = cudaMemsetAsync(reps, 0, static_cast<size_t>(B * V) * 2, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(idx, 0, static_cast<size_t>(B * V) * 4, st);
+    if (e == cudaSuccess && idx != nullptr)
+      e = cudaMemsetAsync(idx, 0, static_cast<size_t>(B * V) * 4, st);
     return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "cudaMemsetAsync");
   }
   return launch_fwd_tc(dtype, hidden, weight, bias, b, s, d, v, reps, idx, ws, st);

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(256)
       const bool pos = logit > 0.f;
       const size_t o = static_cast<size_t>(b) * V + v;
       reps[o] = pos ? log1pf(logit) : 0.f;
-      idx[o] = pos ? best_idx : 0;
+      if (idx != nullptr) idx[o] = pos ? best_idx : 0;
     }
   }
 }

@@ -15,34 +15,22 @@
 // __device__ variable: every GPU that loads the library holds one copy until
 // the process exits. Host code must not pass the variable's name to a kernel
 // (on the host it is only a stand-in symbol); its device address is looked up
-// with cudaGetSymbolAddress the first time the entry point runs on a device,
-// with that device current, and cached per device.
-#include <mutex>
-
+// with cudaGetSymbolAddress on every call, with the calling device current.
+// The lookup is not cached: after a cudaDeviceReset (or any teardown of the
+// primary context) the module is loaded again and the array may sit at a
+// different address, so a cached pointer could go stale.
 #include "internal.h"
 
 namespace {
 
 static __device__ __align__(256) unsigned char g_fwd_scratch[SPARTON_FWD_NOALLOC_SCRATCH_BYTES];
 
-std::mutex g_scratch_mu;
-void* g_scratch_addr[64] = {};
-
-// Device address of this device's copy of g_fwd_scratch (looked up once).
+// Device address of the current device's copy of g_fwd_scratch.
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return sparton::cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64)
-    return sparton::fail(SPARTON_ERR_DEVICE, "sparton_fwd_noalloc supports device ordinals < 64");
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_fwd_scratch);
-    if (e != cudaSuccess) return sparton::cuda_fail(e, "cudaGetSymbolAddress(fwd scratch)");
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_fwd_scratch);
+  if (e != cudaSuccess) return sparton::cuda_fail(e, "cudaGetSymbolAddress(fwd scratch)");
+  *out = p;
   return SPARTON_OK;
 }
 
@@ -52,12 +40,13 @@ extern "C" int sparton_fwd_noalloc(const void* hidden, const void* weight, const
                                    const void* mask, int mask_dtype, int dtype, int64_t B,
                                    int64_t S, int64_t D, int64_t V, void* reps, int32_t* idx,
                                    void* stream) {
-  if (B < 0 || S < 0 || D < 0 || V < 0)
-    return sparton::fail(SPARTON_ERR_INVALID_ARGUMENT, "negative size (B=%lld S=%lld D=%lld V=%lld)",
-                         (long long)B, (long long)S, (long long)D, (long long)V);
-  if (B > (1ll << 24) || S > (1ll << 24))
-    return sparton::fail(SPARTON_ERR_UNSUPPORTED, "sizes out of range (B=%lld S=%lld)",
-                         (long long)B, (long long)S);
+  // The same argument checks as sparton_fwd, before anything touches the
+  // device: a bad size or dtype, or a device that is not sm_100, is reported
+  // as such rather than as a failed symbol lookup.
+  int st = sparton::check_sizes(B, S, D, V);
+  if (st != SPARTON_OK) return st;
+  st = sparton::check_dtype(dtype);
+  if (st != SPARTON_OK) return st;
   const size_t need = sparton::fwd_workspace_bytes(B, S);
   if (need > SPARTON_FWD_NOALLOC_SCRATCH_BYTES)
     return sparton::fail(SPARTON_ERR_UNSUPPORTED,
@@ -65,11 +54,23 @@ extern "C" int sparton_fwd_noalloc(const void* hidden, const void* weight, const
                          "library's fixed scratch holds %zu; use sparton_fwd with a workspace",
                          (long long)B, (long long)S, need,
                          (size_t)SPARTON_FWD_NOALLOC_SCRATCH_BYTES);
+  st = sparton::check_device();
+  if (st != SPARTON_OK) return st;
   void* ws = nullptr;
-  const int st = scratch_address(&ws);
+  st = scratch_address(&ws);
   if (st != SPARTON_OK) return st;
   // The forward resets everything in the scratch that must start at zero (the
   // status word) and overwrites the bits / extents it reads.
   return sparton_fwd(hidden, weight, bias, mask, mask_dtype, dtype, B, S, D, V, reps, idx, ws,
                      SPARTON_FWD_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int sparton_fwd_noalloc_status(void* stream, uint32_t* code) {
+  if (code == nullptr) return sparton::fail(SPARTON_ERR_INVALID_ARGUMENT, "code is NULL");
+  const int st = sparton::check_device();
+  if (st != SPARTON_OK) return st;
+  void* ws = nullptr;
+  const int s2 = scratch_address(&ws);
+  if (s2 != SPARTON_OK) return s2;
+  return sparton_read_device_status(ws, stream, code);
 }

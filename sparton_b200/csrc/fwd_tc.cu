@@ -345,6 +345,8 @@ __device__ void run_mma(const FwdTcParams& p, const Partition& q, uint32_t stage
 
 // Folds the columns of one TMEM chunk selected by `mw` into the running masked
 // max / first argmax; column q of the chunk is position pos0 + q of the row.
+// kIdx false (inference forward, no idx output): the max alone.
+template <bool kIdx>
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw, int pos0,
                                            float& best, int& best_idx) {
   if (mw == 0u) return;
@@ -355,6 +357,10 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw,
   } else {
 #pragma unroll
     for (int q = 0; q < 32; ++q) cm = ((mw >> q) & 1u) ? fmaxf(cm, __uint_as_float(r[q])) : cm;
+  }
+  if (!kIdx) {
+    best = fmaxf(best, cm);
+    return;
   }
   if (cm > best) {
     int first = 31;
@@ -369,7 +375,7 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], uint32_t mw,
 // Per-thread state of the epilogue inside one unit: the current row and its
 // running max. Rows are visited in order; empty rows (no packed columns) are
 // written as the empty-row value when the walk passes them.
-template <typename T>
+template <typename T, bool kIdx>
 struct RowWalk {
   int b;         // current row (below the group's first row: none yet)
   int nxt;       // the next row with columns (the group's end: none)
@@ -390,7 +396,7 @@ struct RowWalk {
       const bool pos = logit > 0.f;
       const size_t o = static_cast<size_t>(row) * p.V + v;
       static_cast<T*>(p.reps)[o] = from_float<T>(pos ? log1pf(logit) : 0.f);
-      p.idx[o] = pos ? best_idx : 0;
+      if (kIdx) p.idx[o] = pos ? best_idx : 0;
     }
   }
   // Stores the current row (if any), then every (empty) row before `upto`.
@@ -424,21 +430,21 @@ __device__ __forceinline__ uint32_t chunk_bits(uint32_t words, int ch, int sh, i
 
 // One 32-column chunk at packed column cc: valid bits `mw`, row starts `rs`
 // (rows start at multiples of 16, so only bits 0 and 16 can be set).
-template <typename T>
+template <typename T, bool kIdx>
 __device__ __forceinline__ void epi_chunk(const FwdTcParams& p, const uint32_t (&r)[32],
                                           uint32_t mw, uint32_t rs, int cc, int first_row,
-                                          RowWalk<T>& w) {
+                                          RowWalk<T, kIdx>& w) {
   if (rs & 1u) w.next_row(p, first_row, cc);
   if (rs & 0x10000u) {
-    scan_chunk(r, mw & 0xFFFFu, cc - w.row_base, w.best, w.best_idx);
+    scan_chunk<kIdx>(r, mw & 0xFFFFu, cc - w.row_base, w.best, w.best_idx);
     w.next_row(p, first_row, cc + 16);
-    scan_chunk(r, mw & 0xFFFF0000u, cc - w.row_base, w.best, w.best_idx);
+    scan_chunk<kIdx>(r, mw & 0xFFFF0000u, cc - w.row_base, w.best, w.best_idx);
   } else {
-    scan_chunk(r, mw, cc - w.row_base, w.best, w.best_idx);
+    scan_chunk<kIdx>(r, mw, cc - w.row_base, w.best, w.best_idx);
   }
 }
 
-template <typename T>
+template <typename T, bool kIdx>
 __device__ void run_epilogue(const FwdTcParams& p, const Partition& q, uint32_t tmem_base,
                              const Ctrl& c, int warp, int lane) {
   const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
@@ -449,7 +455,7 @@ __device__ void run_epilogue(const FwdTcParams& p, const Partition& q, uint32_t 
   for (bool more = u.start(p, q); more; more = u.advance(p, q)) {
     const Unit& un = u.cur;
     const int g_begin = un.r0, g_end = un.r1;
-    RowWalk<T> w;
+    RowWalk<T, kIdx> w;
     w.b = g_begin - 1;
     w.kk = un.k0;
     w.k_end = un.k1;
@@ -488,13 +494,13 @@ __device__ void run_epilogue(const FwdTcParams& p, const Partition& q, uint32_t 
         tmem_ld_wait(ra);
         if (ch + 1 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 1)), rb);
         const int left0 = un.c1 - (t0 + 32 * ch);
-        epi_chunk<T>(p, ra, chunk_bits(vwords, ch, wsh, left0),
+        epi_chunk<T, kIdx>(p, ra, chunk_bits(vwords, ch, wsh, left0),
                      chunk_bits(swords, ch, wsh, left0), t0 + 32 * ch, g_begin, w);
         if (ch + 1 < nch) {
           tmem_ld_wait(rb);
           if (ch + 2 < nch) tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(32 * (ch + 2)), ra);
           const int left1 = un.c1 - (t0 + 32 * (ch + 1));
-          epi_chunk<T>(p, rb, chunk_bits(vwords, ch + 1, wsh, left1),
+          epi_chunk<T, kIdx>(p, rb, chunk_bits(vwords, ch + 1, wsh, left1),
                        chunk_bits(swords, ch + 1, wsh, left1), t0 + 32 * (ch + 1), g_begin, w);
         }
       }
@@ -559,7 +565,7 @@ __device__ Partition choose_partition(const FwdTcParams& p, float* red_cost, int
   return q;
 }
 
-template <typename T, uint32_t kFmt>
+template <typename T, uint32_t kFmt, bool kIdx>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ HiddenMaps tmH,
                   const FwdTcParams p) {
@@ -611,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     run_mma<kFmt>(p, q, stage_base, tmem_base, c);
     __syncwarp();
   } else {
-    run_epilogue<T>(p, q, tmem_base, c, warp, lane);
+    run_epilogue<T, kIdx>(p, q, tmem_base, c, warp, lane);
   }
 
   tc_fence_before_sync();
@@ -627,6 +633,29 @@ int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint
                 uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
   return make_tensor_map_2d(map, dt, base, inner, outer, inner * 2, box_inner, box_outer,
                             CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename T, uint32_t kFmt, bool kIdx>
+int launch_kernel(const CUtensorMap& tmW, const HiddenMaps& tmH, const FwdTcParams& p,
+                  unsigned grid, cudaStream_t stream) {
+  static std::mutex mu;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !attr_done[dev]) {
+      e = cudaFuncSetAttribute(fwd_tc_kernel<T, kFmt, kIdx>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd_tc_kernel)");
+      attr_done[dev] = true;
+    }
+  }
+  fwd_tc_kernel<T, kFmt, kIdx><<<grid, kThreads, kSmemBytes, stream>>>(tmW, tmH, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fwd_tc_kernel launch");
+  return SPARTON_OK;
 }
 
 template <typename T, uint32_t kFmt>
@@ -664,29 +693,15 @@ int launch_typed(CUtensorMapDataType dt, const void* hidden, const void* weight,
   p.idx = idx;
   p.status = ws.status;
 
-  static std::mutex mu;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 64 && !attr_done[dev]) {
-      e = cudaFuncSetAttribute(fwd_tc_kernel<T, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSmemBytes);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd_tc_kernel)");
-      attr_done[dev] = true;
-    }
-  }
   // The number of units (vocab tiles x groups) is chosen on the device; there
   // are at most num_vtiles * B of them.
   const long long max_units = static_cast<long long>(p.num_vtiles) * B;
   const long long grid_ll = max_units < device_sm_count() ? max_units : device_sm_count();
   const unsigned grid = static_cast<unsigned>(grid_ll > 0 ? grid_ll : 1);
-  fwd_tc_kernel<T, kFmt><<<grid, kThreads, kSmemBytes, stream>>>(tmW, tmH, p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "fwd_tc_kernel launch");
-  return SPARTON_OK;
+  // Without an idx output (the inference forward) the epilogue keeps the max
+  // only and stores reps alone.
+  return idx != nullptr ? launch_kernel<T, kFmt, true>(tmW, tmH, p, grid, stream)
+                        : launch_kernel<T, kFmt, false>(tmW, tmH, p, grid, stream);
 }
 
 }  // namespace

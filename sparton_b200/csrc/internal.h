@@ -20,6 +20,12 @@ int fail(int status, const char* fmt, ...);
 // Turns a CUDA error into SPARTON_ERR_CUDA with a message naming `what`.
 int cuda_fail(cudaError_t err, const char* what);
 
+// Argument checks shared by the entry points (capi.cu); each records a message
+// and returns a status on failure.
+int check_sizes(int64_t B, int64_t S, int64_t D, int64_t V);  // head sizes B, S, D, V
+int check_dtype(int dtype);                                    // a sparton_dtype value
+int check_device();                                            // current device is sm_100
+
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // 2-D TMA tensor map over a row-major [outer][inner] array with `row_bytes`

@@ -59,11 +59,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // Bounded wait on phase `parity` of a barrier. Returns false when the shared
-// abort flag is raised by another role, or when this wait exceeds
-// kWaitTimeoutNs (then it raises the flag and records `code` in *status).
+// abort flag is raised by another role, or when this wait exceeds `limit_ns`
+// (kWaitTimeoutNs in every production kernel; then it raises the flag and
+// records `code` in *status).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int* abort_flag,
-                                                  unsigned int* status, unsigned int code) {
+                                                  unsigned int* status, unsigned int code,
+                                                  uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
@@ -71,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(status, 0u, code);
       return false;
@@ -98,8 +100,10 @@ __device__ __forceinline__ bool elect_one() {
 // in all of them, so the warp leaves a loop together.
 __device__ __forceinline__ bool mbar_wait_bounded_warp(uint32_t bar, uint32_t parity,
                                                        volatile int* abort_flag,
-                                                       unsigned int* status, unsigned int code) {
-  return __all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar, parity, abort_flag, status, code));
+                                                       unsigned int* status, unsigned int code,
+                                                       uint64_t limit_ns = kWaitTimeoutNs) {
+  return __all_sync(0xFFFFFFFFu,
+                    mbar_wait_bounded(bar, parity, abort_flag, status, code, limit_ns));
 }
 
 // Wait used only while unwinding after an abort: ignores the abort flag but

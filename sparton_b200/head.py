@@ -238,11 +238,58 @@ class SpartonHead(nn.Module):
         return self.shard.world_size > 1
 
     def tie_weights(self, decoder):
-        """Alias the decoder's Parameters (upstream :721-723). With a process
-        group the full Parameters are kept and each rank uses its row range, so
-        their .grad is full-size with zeros outside the shard."""
-        self.weight = decoder.weight
-        self.bias = decoder.bias
+        """Alias the decoder's Parameters (upstream :721-723).
+
+        With a process group (vocabulary-sharded) the head's ``weight`` /
+        ``bias`` become Parameters over this rank's rows of the decoder's
+        tensors: views that share the decoder's storage, so an optimizer step
+        on the head writes straight into those rows, while the gradient the
+        head accumulates is shard-sized ([V_s, D], not a full [V, D] that is
+        zero outside the shard). The decoder's own full Parameters then get no
+        gradient from the head, and their rows outside this rank's shard are
+        not updated here: ``gather_weights()`` assembles the full, current
+        tensors (for a checkpoint, or to refresh the decoder)."""
+        if not self.sharded:
+            self.weight = decoder.weight
+            self.bias = decoder.bias
+            return
+        sh = self.shard
+        if decoder.weight.shape[0] != self.vocab_size:
+            raise ValueError(f"decoder has {decoder.weight.shape[0]} rows, head vocab_size "
+                             f"{self.vocab_size}")
+        self.weight = nn.Parameter(decoder.weight.detach().narrow(0, sh.start, sh.size))
+        self.bias = (nn.Parameter(decoder.bias.detach().narrow(0, sh.start, sh.size))
+                     if decoder.bias is not None else None)
+
+    @torch.no_grad()
+    def gather_weights(self, out_weight: Optional[torch.Tensor] = None,
+                       out_bias: Optional[torch.Tensor] = None):
+        """(weight [V, D], bias [V] or None): the full parameters assembled from
+        every rank's shard (all-gather over the head's group; every rank must
+        call it). Unsharded: the head's own tensors. ``out_weight`` /
+        ``out_bias`` (e.g. a tied decoder's full Parameters) receive the result
+        in place; a checkpoint saved after this holds the trained rows of every
+        shard."""
+        if not self.sharded:
+            w, b = self.weight.detach(), (self.bias.detach() if self.bias is not None else None)
+        else:
+            w = self._gather_rows(self.weight.detach())
+            b = self._gather_rows(self.bias.detach()) if self.bias is not None else None
+        if out_weight is not None:
+            out_weight.copy_(w)
+            w = out_weight
+        if out_bias is not None and b is not None:
+            out_bias.copy_(b)
+            b = out_bias
+        return w, b
+
+    def _gather_rows(self, local: torch.Tensor) -> torch.Tensor:
+        sh = self.shard
+        buf = local.new_zeros((sh.padded,) + tuple(local.shape[1:]))
+        buf[: local.shape[0]] = local
+        parts = [torch.empty_like(buf) for _ in range(sh.world_size)]
+        dist.all_gather(parts, buf.contiguous(), group=self.process_group)
+        return torch.cat(parts, dim=0)[: self.vocab_size].contiguous()
 
     def load(self, weights_dict):
         """Copy ``weights_dict["weight"]`` (and ``["bias"]``) in place (upstream
@@ -278,6 +325,17 @@ class SpartonHead(nn.Module):
 
     def forward(self, hidden_states, attention_mask):
         weight, bias = self._local_params()
+        if not (torch.is_grad_enabled() and any(
+                t is not None and t.requires_grad for t in (hidden_states, weight, bias))):
+            # Nothing will flow back (no_grad / inference_mode, e.g. an encode
+            # for indexing): the forward without the argmax output, which
+            # skips the [B, V] int32 idx. Same reps. Sharded, no collective is
+            # involved either way.
+            reps = torch.ops.sparton.fused_sparton_fwd_scores(hidden_states, weight, bias,
+                                                             attention_mask)
+            if self.sharded and self.gather_output:
+                reps = _GatherVocab.apply(reps, self.shard, self.process_group)
+            return reps
         if not self.sharded:
             scores, _idx = torch.ops.sparton.fused_sparton_fwd(hidden_states, weight, bias,
                                                                attention_mask)

@@ -66,7 +66,11 @@ def _check_fwd_args(hidden, embed, bias, mask) -> None:
 
 
 def forward_impl(hidden: torch.Tensor, embed: torch.Tensor, bias: Optional[torch.Tensor],
-                 mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+                 mask: torch.Tensor, with_idx: bool = True
+                 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """(reps, idx); with ``with_idx=False`` the inference forward: the kernel
+    keeps the max alone, stores reps only and idx is None (no [B, V] int32 is
+    allocated or written)."""
     _check_fwd_args(hidden, embed, bias, mask)
     lib = _lib.load()
     B, S, D = hidden.shape
@@ -77,7 +81,7 @@ def forward_impl(hidden: torch.Tensor, embed: torch.Tensor, bias: Optional[torch
     mask = kernel_mask(mask)
     dev = hidden.device
     reps = torch.empty((B, V), dtype=hidden.dtype, device=dev)
-    idx = torch.empty((B, V), dtype=torch.int32, device=dev)
+    idx = torch.empty((B, V), dtype=torch.int32, device=dev) if with_idx else None
     ws = torch.empty(lib.sparton_fwd_workspace_size(B, S, D, V), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         st = lib.sparton_fwd(_lib.ptr(hidden), _lib.ptr(embed), _lib.ptr(bias), _lib.ptr(mask),
@@ -241,3 +245,19 @@ def _backward(ctx, grad_scores, grad_idx):
 
 
 fused_sparton_fwd.register_autograd(_backward, setup_context=_setup_context)
+
+
+@torch.library.custom_op("sparton::fused_sparton_fwd_scores", mutates_args=())
+def fused_sparton_fwd_scores(hidden: torch.Tensor, embed: torch.Tensor,
+                             bias: Optional[torch.Tensor], mask: torch.Tensor) -> torch.Tensor:
+    """Inference forward: scores[B,V] of fused_sparton_fwd without the argmax.
+    Upstream's counterpart is its no-argmax ``fused_sparton_fwd`` host function
+    (sparton_kernel.py:372-394, reduce kernel :257-334), meant for ``encode``
+    under ``no_grad`` (training/model.py:141-144). Not differentiable: training
+    uses ``fused_sparton_fwd``, whose idx the backward needs."""
+    return forward_impl(hidden, embed, bias, mask, with_idx=False)[0]
+
+
+@fused_sparton_fwd_scores.register_fake
+def _(hidden, embed, bias, mask):
+    return hidden.new_empty((hidden.shape[0], embed.shape[0]))

@@ -48,3 +48,13 @@ def test_synthetic_inputs_follow_the_config():
     assert (L == 64).float().mean() > 0.05  # the full-length fraction of config 4
     again = bench.make_inputs(c)
     assert torch.equal(H, again[0]) and torch.equal(L, again[5])  # seeded
+
+
+def test_cpu_baseline_runs_the_whole_batch_when_it_fits():
+    c = dict(bench.WORKLOADS["config2"], B=4, S=16, D=32, V=64, lengths=(2, 16))
+    assert bench.cpu_rows_for(c) == 4  # a few KB per row: the whole batch
+    res = bench.cpu_baseline(c, bench.cpu_rows_for(c), steps=1, warmup=1)
+    assert res["kind"] == "port" and not res["extrapolated"] and res["value"] > 0
+    assert "whole batch" in res["sample"] and res["cpu_model"]
+    part = bench.cpu_baseline(c, 2, steps=1, warmup=1)
+    assert part["extrapolated"] and "extrapolated" in part["sample"]

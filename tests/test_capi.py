@@ -132,3 +132,18 @@ def test_components_validate_before_any_launch(lib):
         _lib.ERR_UNSUPPORTED
     # regularisers: small workspace
     assert lib.sparton_reg_fwd(d, 2, 4, 100, 1.0, 1.0, d, d, ws, 1, None) == _lib.ERR_WORKSPACE
+
+
+def test_noalloc_checks_arguments_before_the_device(lib):
+    """sparton_fwd_noalloc validates sizes, dtype and its scratch limit before
+    it looks at the device (no GPU here): each is reported as itself."""
+    dummy = ctypes.c_void_p(0x1000)
+    assert lib.sparton_fwd_noalloc(dummy, dummy, None, dummy, 2, 2, -1, 8, 16, 10, dummy, dummy,
+                                   None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.sparton_fwd_noalloc(dummy, dummy, None, dummy, 2, 7, 2, 8, 16, 10, dummy, dummy,
+                                   None) == _lib.ERR_UNSUPPORTED
+    assert "dtype" in _lib.last_error()
+    assert lib.sparton_fwd_noalloc(dummy, dummy, None, dummy, 2, 2, 4096, 8192, 64, 100, dummy,
+                                   dummy, None) == _lib.ERR_UNSUPPORTED
+    assert "scratch" in _lib.last_error()
+    assert lib.sparton_fwd_noalloc_status(None, None) == _lib.ERR_INVALID_ARGUMENT

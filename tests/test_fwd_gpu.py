@@ -177,3 +177,29 @@ def test_rejects_cpu_tensors_and_bad_shapes():
         torch.ops.sparton.fused_sparton_fwd(H.cuda(), W[:, :32].cuda(), b.cuda(), mask.cuda())
     with pytest.raises(ValueError):
         torch.ops.sparton.fused_sparton_fwd(H.cuda(), W.float().cuda(), b.cuda(), mask.cuda())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_inference_forward_without_idx(dtype):
+    """The inference forward (idx NULL through the C ABI, the
+    fused_sparton_fwd_scores op) writes the same reps as the training forward,
+    bit for bit, and SpartonHead takes it when autograd is off."""
+    from sparton_b200.head import SpartonHead
+
+    B, S, D, V = 9, 300, 256, 1100
+    H, W, b, mask, _ = synthetic(B, S, D, V, (0, 300), dtype=dtype, seed=41, w_std=0.03)
+    dev = torch.device("cuda")
+    Hd, Wd, bd, md = H.to(dev), W.to(dev), b.to(dev), mask.to(dev)
+    reps, idx = torch.ops.sparton.fused_sparton_fwd(Hd, Wd, bd, md)
+    scores = torch.ops.sparton.fused_sparton_fwd_scores(Hd, Wd, bd, md)
+    torch.cuda.synchronize()
+    assert torch.equal(scores.cpu(), reps.cpu())
+    head = SpartonHead(V, D, use_bias=True).to(dev, dtype)
+    head.load({"weight": Wd, "bias": bd})
+    with torch.no_grad():
+        r_nograd = head(Hd, md)
+    with torch.inference_mode():
+        r_inf = head(Hd, md)
+    assert not r_nograd.requires_grad
+    assert torch.equal(r_nograd.cpu(), reps.cpu()) and torch.equal(r_inf.cpu(), reps.cpu())
+    check_fwd(H, W, b, mask, scores.cpu(), idx.cpu())

@@ -1,9 +1,12 @@
-"""Vocabulary-sharded SpartonHead on 2 GPUs (NCCL), against the same head on
-one GPU: the forward shards and the d_weight / d_bias shards are bit-identical
-(every vocab column is computed by the same kernel arithmetic whichever rank
-owns it); d_hidden, an all-reduce of fp32 partial sums, matches within one bf16
-rounding (rtol 1e-2) plus 1e-2 of its largest entry. Run with the all-reduce in
-one chunk and one batch row per chunk. Skipped with fewer than 2 GPUs."""
+"""Vocabulary-sharded SpartonHead on 2 and 4 GPUs (NCCL), against the same head
+on one GPU: the forward shards and the d_weight / d_bias shards are
+bit-identical (every vocab column is computed by the same kernel arithmetic
+whichever rank owns it); d_hidden, an all-reduce of fp32 partial sums, matches
+within one bf16 rounding (rtol 1e-2) plus 1e-2 of its largest entry. Run with
+the all-reduce in one chunk, with one batch row per chunk, and with the head
+tied to a full nn.Linear decoder (tie_weights: shard-sized gradients that land
+in the decoder's rows). V = 3001 leaves a ragged last shard at every world
+size. Skipped with fewer GPUs than ranks."""
 import os
 import socket
 
@@ -39,16 +42,25 @@ def _worker(rank, world, port, out_dir):
     try:
         H, W, b, mask, g = synthetic(B, S, D, V, (20, S), dtype=torch.bfloat16, seed=5,
                                      w_std=0.06)
-        for tag, chunk in (("one", 128 << 20), ("rows", 1)):
+        for tag, chunk in (("one", 128 << 20), ("rows", 1), ("tied", 128 << 20)):
             head_mod.REDUCE_CHUNK_BYTES = chunk
             head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD).to(
                 dev, torch.bfloat16)
             sh = head.shard
-            head.load({"weight": W[sh.start:sh.stop], "bias": b[sh.start:sh.stop]})
+            if tag == "tied":
+                decoder = torch.nn.Linear(D, V).to(dev, torch.bfloat16)
+                with torch.no_grad():
+                    decoder.weight.copy_(W)
+                    decoder.bias.copy_(b)
+                head.tie_weights(decoder)
+                assert head.weight.shape == (sh.size, D)
+            else:
+                head.load({"weight": W[sh.start:sh.stop], "bias": b[sh.start:sh.stop]})
             hid = H.to(dev).requires_grad_(True)
             reps = head(hid, mask.to(dev))
             reps.backward(g[:, sh.start:sh.stop].to(dev))
             torch.cuda.synchronize(dev)
+            assert head.weight.grad.shape == (sh.size, D)
             torch.save({"reps": reps.detach().cpu(), "dH": hid.grad.cpu(),
                         "dW": head.weight.grad.cpu(), "db": head.bias.grad.cpu(),
                         "shard": (sh.start, sh.stop)},
@@ -58,11 +70,12 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_head_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_head_matches_single_gpu(tmp_path, world):
     from sparton_b200.head import SpartonHead
 
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
     H, W, b, mask, g = synthetic(B, S, D, V, (20, S), dtype=torch.bfloat16, seed=5, w_std=0.06)
@@ -74,7 +87,7 @@ def test_sharded_head_matches_single_gpu(tmp_path):
     reps.backward(g.to(dev))
     ref = {"reps": reps.detach().cpu(), "dH": hid.grad.cpu(), "dW": head.weight.grad.cpu(),
            "db": head.bias.grad.cpu()}
-    for tag in ("one", "rows"):
+    for tag in ("one", "rows", "tied"):
         covered = 0
         for r in range(world):
             got = torch.load(tmp_path / f"r{r}_{tag}.pt")

@@ -159,3 +159,61 @@ def test_sharded_head_two_ranks(tmp_path):
         for r in range(world):
             np.testing.assert_allclose(np.load(tmp_path / f"r{r}_rs{rows}_dH.npy"), dH32,
                                        rtol=1e-5, atol=1e-6)
+
+
+def _tie_worker(rank, world, port, out_dir):
+    """Sharded tie_weights: the head trains this rank's rows of the decoder's
+    storage with a shard-sized gradient; gather_weights assembles the full
+    tensors after each rank updated its rows."""
+    from torch import nn
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ops.forward_impl = _cpu_forward
+        ops.backward_impl = _cpu_backward
+        ops.hidden_grad_rows = _cpu_hidden_rows
+        H, W, b, mask, g = _inputs()
+        decoder = nn.Linear(D, V).double()
+        with torch.no_grad():
+            decoder.weight.copy_(W)
+            decoder.bias.copy_(b)
+        head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD).double()
+        head.tie_weights(decoder)
+        sh = head.shard
+        assert head.weight.shape == (sh.size, D) and head.bias.shape == (sh.size,)
+        assert head.weight.data_ptr() == decoder.weight[sh.start].data_ptr()
+        hid = H.clone().requires_grad_(True)
+        head(hid, mask).backward(g[:, sh.start:sh.stop])
+        assert head.weight.grad.shape == (sh.size, D)  # shard-sized, not [V, D]
+        assert decoder.weight.grad is None
+        with torch.no_grad():  # an optimizer step on the shard lands in the decoder's rows
+            head.weight.add_(1.0)
+            head.bias.add_(1.0)
+        assert torch.equal(decoder.weight[sh.start:sh.stop], W[sh.start:sh.stop] + 1.0)
+        full_w, full_b = head.gather_weights(out_weight=decoder.weight.data,
+                                             out_bias=decoder.bias.data)
+        np.save(os.path.join(out_dir, f"tie_r{rank}_w.npy"), full_w.numpy())
+        np.save(os.path.join(out_dir, f"tie_r{rank}_b.npy"), full_b.numpy())
+        np.save(os.path.join(out_dir, f"tie_r{rank}_dW.npy"), head.weight.grad.numpy())
+        np.save(os.path.join(out_dir, f"tie_r{rank}_shard.npy"), np.array([sh.start, sh.stop]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_tie_weights_keeps_shard_sized_grads(tmp_path):
+    world = 2
+    mp.start_processes(_tie_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    H, W, b, mask, g = _inputs()
+    reps, idx, _ = orc.forward(H.numpy(), W.numpy(), b.numpy(), mask.numpy())
+    _, dW, _ = orc.backward_from_scores(g.numpy(), reps, idx, H.numpy(), W.numpy(), True)
+    for r in range(world):
+        lo, hi = np.load(tmp_path / f"tie_r{r}_shard.npy")
+        np.testing.assert_allclose(np.load(tmp_path / f"tie_r{r}_dW.npy"), dW[lo:hi], rtol=1e-10,
+                                   atol=1e-12)
+        # every rank added 1 to its own rows: the gathered tensors are W + 1 everywhere
+        np.testing.assert_allclose(np.load(tmp_path / f"tie_r{r}_w.npy"), W.numpy() + 1.0,
+                                   rtol=0, atol=0)
+        np.testing.assert_allclose(np.load(tmp_path / f"tie_r{r}_b.npy"), b.numpy() + 1.0,
+                                   rtol=0, atol=0)

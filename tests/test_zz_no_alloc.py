@@ -9,17 +9,19 @@ into the library, shared by every call on the device.
 
 The test calls the entry point through the C ABI twice in a row, with
 different shapes and masks, and checks each result against sparton_fwd (the
-entry point with a caller workspace) under the forward tests' tolerance
-(reps rtol 1e-2 for bf16; argmax equal). The second call reuses the scratch
-left by the first, so it also shows that nothing stale leaks between calls.
-This file is collected last on purpose.
+entry point with a caller workspace). Both run the same kernels on the same
+inputs, so reps and idx must be bit-identical (torch.equal), and the device
+status word that sparton_fwd_noalloc_status reads back must be 0 after each
+call. The second call reuses the scratch left by the first, so it also shows
+that nothing stale leaks between calls. This file is collected last on purpose.
 """
-import numpy as np
+import ctypes
+
 import pytest
 import torch
 
 from sparton_b200 import _lib
-from tests._cases import np64, synthetic
+from tests._cases import synthetic
 
 pytestmark = pytest.mark.gpu
 
@@ -65,8 +67,13 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         H, W, b, mask = H.to(dev), W.to(dev), b.to(dev), mask.to(dev)
         ref_reps, ref_idx = _with_workspace(lib, H, W, b, mask)
         reps, idx = _without_workspace(lib, H, W, b, mask)
+        code = ctypes.c_uint32(0xFFFFFFFF)
+        _lib.check(lib.sparton_fwd_noalloc_status(torch.cuda.current_stream().cuda_stream,
+                                                  ctypes.byref(code)),
+                   "sparton_fwd_noalloc_status")
+        assert code.value == 0, f"device status {code.value:#x} after sparton_fwd_noalloc"
         torch.cuda.synchronize()
-        np.testing.assert_allclose(np64(reps.cpu()), np64(ref_reps.cpu()), rtol=1e-2, atol=1e-3)
+        assert torch.equal(reps.cpu(), ref_reps.cpu())
         assert torch.equal(idx.cpu(), ref_idx.cpu())
 
 
