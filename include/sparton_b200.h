@@ -277,6 +277,35 @@ int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, cons
                           void* d_gamma, void* d_beta, void* d_bias, void* workspace,
                           size_t workspace_size, void* stream);
 
+/* ------------------------------------------------------------------ GEMM */
+/* The contractions around the head on the same tcgen05 tensor-core machinery
+ * as the forward: the dense layer of the MLM transform and its two backward
+ * products (training/model.py:25-35, used at :82-85), and the InfoNCE scores
+ * q_reps @ d_reps.T and their backward (training/train.py:73-77). Upstream
+ * runs them as torch matmuls (cuBLAS); this entry point replaces those calls.
+ *
+ *   C[m, n] = sum_k A[m, k] * B[n, k]  (+ bias[n])      fp32 sums
+ *
+ * Operand layouts (dense, row-major in memory):
+ *   SPARTON_LAYOUT_ROWS: A stored [M][K], B stored [N][K] (contraction index
+ *                        contiguous; y = x @ W.T has A = x, B = W);
+ *   SPARTON_LAYOUT_COLS: A stored [K][M], B stored [K][N] (output index
+ *                        contiguous; dx = dy @ W has B = W stored [K][N],
+ *                        dW = dy.T @ x has A = dy, B = x stored [K][*]).
+ * A, B and bias [N] are `dtype` (bf16 or f16); C [M][ldc] is `c_dtype` (dtype
+ * or F32). The contiguous dimension of each operand must be a multiple of 8
+ * (16-byte rows for the TMA loads); 0 < K. Long contractions over few output
+ * tiles are split over the K range and the splits added in a fixed order
+ * (deterministic); the workspace (256-byte aligned) holds those partials. */
+#define SPARTON_LAYOUT_ROWS 0
+#define SPARTON_LAYOUT_COLS 1
+
+size_t sparton_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+
+int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const void* bias,
+                 int dtype, int64_t M, int64_t N, int64_t K, void* C, int c_dtype, int64_t ldc,
+                 void* workspace, size_t workspace_size, void* stream);
+
 /* --------------------------------------------------------------- status */
 
 /* Copies the device status word of a workspace used by sparton_fwd /

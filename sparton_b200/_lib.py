@@ -22,6 +22,9 @@ ERR_WORKSPACE = 3
 ERR_CUDA = 4
 ERR_DEVICE = 5
 
+# operand layouts of sparton_gemm
+LAYOUT_ROWS = 0
+LAYOUT_COLS = 1
 # sparton_dtype
 DTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 # sparton_mask_dtype
@@ -52,6 +55,8 @@ EXPORTED_SYMBOLS = (
     "sparton_transform_bwd",
     "sparton_read_device_status",
     "sparton_selftest_wait_timeout",
+    "sparton_gemm_workspace_size",
+    "sparton_gemm",
 )
 
 _lock = threading.Lock()
@@ -109,6 +114,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_read_device_status.restype = _i
     lib.sparton_selftest_wait_timeout.argtypes = [ctypes.c_uint32, _vp, _sz, _vp]
     lib.sparton_selftest_wait_timeout.restype = _i
+    lib.sparton_gemm_workspace_size.argtypes = [_i64, _i64, _i64]
+    lib.sparton_gemm_workspace_size.restype = _sz
+    lib.sparton_gemm.argtypes = [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _i64, _vp, _i, _i64, _vp,
+                                 _sz, _vp]
+    lib.sparton_gemm.restype = _i
 
 
 def load() -> ctypes.CDLL:

@@ -9,11 +9,10 @@
 //
 // Here every output element is produced by exactly one warp in a fixed order
 // (deterministic, no atomics):
-//   K2 bwd_sort_kernel   per batch row (a cluster of up to 8 CTAs, combined
-//                        through distributed shared memory): stable counting
-//                        sort of the vocab ids with score > 0 by argmax
-//                        position -> CSR (offs[b][s]) of (v, g') pairs, v
-//                        ascending inside each bucket.
+//   K2 sort_*_kernel     stable counting sort of each batch row's vocab ids
+//                        with score > 0 by argmax position -> CSR
+//                        (offs[b][s]) of (v, g') pairs, v ascending inside
+//                        each bucket: chunk counts, a per-row scan, a scatter.
 //      dw_list_kernel    tiled transpose of (argmax row, g') to vocab-major
 //                        order: the B entries of each vocab id, contiguous.
 //   K3 gather_kernel<0>  one warp per (b, s) row: dH[b,s,:] = sum over its
@@ -31,8 +30,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
-
-#include <cooperative_groups.h>
 
 #include <mutex>
 #include <type_traits>
@@ -130,148 +127,221 @@ __device__ __forceinline__ void store8(O* p, const float (&x)[8]) {
 }
 
 // ------------------------------------------------------------------ K2: sort
-// A thread-block cluster of P CTAs (P = 1, 2, 4 or 8) per batch row, `nw`
-// warps each. CTA c of the cluster owns the vocab range [c*part, (c+1)*part)
-// and warp w of it the contiguous sub-range [w*chunk, (w+1)*chunk), with a row
-// `cnt[w][0..S)` of the CTA's shared table.
-//   pass 1: cnt[w][s] = number of entries of warp w with argmax s
-//   scan:   tot[s] = this CTA's column sum; cnt[w][s] becomes the prefix over
-//           the warps before w. After a cluster barrier every CTA reads all
-//           CTAs' tot[] through distributed shared memory: base[s] = sum over
-//           the CTAs before it, full[s] = sum over all of them (a second
-//           cluster barrier keeps every tot[] alive until all reads are done).
-//           offs[b][s] = exclusive prefix over s of full[]; warp w of CTA c
-//           starts bucket s at offs[b][s] + base[s] + cnt[w][s].
-//   pass 2: each warp replays its range in order and writes (v, g') at its
-//           slot + (rank among lower lanes with the same s) -> stable, v
-//           ascending inside each bucket.
+// Stable counting sort of every batch row's vocab ids with reps > 0 by their
+// argmax position, in three short kernels over chunks of `chunk` consecutive
+// vocab ids (nw warps x 128 ids; nw from S so that the per-warp tables fit in
+// shared memory):
+//   sort_count_kernel   one CTA per (chunk, row): cnt[b][c][s] = entries of
+//                       chunk c with argmax s (shared-memory histogram);
+//   sort_scan_kernel    one CTA per row: cnt[b][c][s] becomes the exclusive
+//                       prefix over the chunks before c, and offs[b][s] the
+//                       exclusive prefix over positions of the bucket sizes;
+//   sort_scatter_kernel one CTA per (chunk, row): per-warp counts per position
+//                       (16-bit), their prefix over the warps of the CTA, then
+//                       every warp replays its 128 ids in order and writes
+//                       (v, g') at offs[b][s] + cnt[b][c][s] + (warp prefix) +
+//                       (earlier entries of the warp with that s) + (lower lanes
+//                       with that s): v ascending inside every bucket, the same
+//                       CSR as a sequential stable sort.
+// No cluster barriers or grid-wide waits: each kernel's CTAs are independent.
+constexpr int kSortWarpIds = 128;                 // vocab ids per warp in a chunk
+constexpr int kSortIters = kSortWarpIds / 32;     // entries per lane
+constexpr int kSortSmemBudget = 220 * 1024;       // scatter: nw x S 16-bit + S int32
+constexpr int kSortMaxS = kSortSmemBudget / 6;    // nw >= 1
+
+__host__ __device__ inline int sort_warps(int S) {
+  int nw = 8;
+  while (nw > 1 && (nw * 2 + 4) * S > kSortSmemBudget) nw >>= 1;
+  return nw;
+}
+
+// Lanes of the warp whose key equals this lane's (keys in [0, 2^nbits), or -1
+// for "no entry", which forms its own group): one ballot per key bit. Used
+// instead of __match_any_sync, which issues on a slow pipe (the sort kernels
+// built on it were bound by that pipe).
+__device__ __forceinline__ unsigned same_key_lanes(int key, int nbits) {
+  unsigned m = __ballot_sync(0xFFFFFFFFu, key >= 0);
+  if (key < 0) m = ~m;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1;
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, bit);
+    m &= bit ? bal : ~bal;
+  }
+  return m;
+}
+
+__device__ __forceinline__ int key_bits(int S) { return S > 1 ? 32 - __clz(S - 1) : 0; }
+
 template <typename T>
-__global__ void __launch_bounds__(1024)
-    bwd_sort_kernel(const T* __restrict__ g, const T* __restrict__ reps,
-                    const int32_t* __restrict__ idx, int S, int V, int* __restrict__ offs,
-                    int2* __restrict__ ent, unsigned int* status,
-                    unsigned int* row_counter) {
-  extern __shared__ int cnt[];  // [nw][S], then tot[S] and, when P > 1, base[S], full[S]
-  __shared__ int scan_tmp[33];
-  namespace cg = cooperative_groups;
-  const cg::cluster_group cluster = cg::this_cluster();
-  const int P = static_cast<int>(cluster.num_blocks());
-  const int c = static_cast<int>(cluster.block_rank());
-  const int b = blockIdx.y;
-  const int nw = blockDim.x >> 5;
+__device__ __forceinline__ int sort_key(float sc, int s, int S) {
+  return (sc > 0.f && s >= 0 && s < S) ? s : -1;
+}
+
+// The sort keys of one warp's 128 vocab ids, lane-strided (entry i of this
+// lane is vocab id v_begin + 32 i + lane), all loads issued before any use.
+template <typename T>
+__device__ __forceinline__ void sort_load_keys(const T* reps, const int32_t* idx, size_t row,
+                                               int v_begin, int v_end, int S, int lane,
+                                               int (&key)[kSortIters], float (&sc)[kSortIters]) {
+  int s[kSortIters];
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i) {
+    const int v = v_begin + 32 * i + lane;
+    sc[i] = v < v_end ? ldg_f32<T>(reps + row + v) : 0.f;
+    s[i] = v < v_end ? __ldg(idx + row + v) : -1;
+  }
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i) key[i] = sort_key<T>(sc[i], s[i], S);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    sort_count_kernel(const T* __restrict__ reps, const int32_t* __restrict__ idx, int S, int V,
+                      int chunk, int n_chunks, int* __restrict__ cnt, unsigned int* status,
+                      unsigned int* row_counter) {
+  extern __shared__ int hist[];  // [S]
+  const int c = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* tot = cnt + nw * S;
-  int* base = tot + S;
-  int* full = P > 1 ? base + S : tot;
-  if (blockIdx.x == 0 && b == 0 && threadIdx.x == 0) {
+  if (c == 0 && b == 0 && threadIdx.x == 0) {
     *status = 0u;
     *row_counter = 0u;
   }
-  for (int i = threadIdx.x; i < nw * S; i += blockDim.x) cnt[i] = 0;
+  const int c_end = min(V, (c + 1) * chunk);
+  const int v_begin = min(c_end, c * chunk + warp * kSortWarpIds);
+  const int v_end = min(c_end, v_begin + kSortWarpIds);
+  int key[kSortIters];
+  float sc[kSortIters];
+  sort_load_keys<T>(reps, idx, static_cast<size_t>(b) * V, v_begin, v_end, S, lane, key, sc);
+  for (int i = threadIdx.x; i < S; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-
-  const int part = (((V + P - 1) / P) + 31) & ~31;
-  const int p_begin = min(V, c * part), p_end = min(V, p_begin + part);
-  const int chunk = (((p_end - p_begin + nw - 1) / nw) + 31) & ~31;
-  const int v_begin = min(p_end, p_begin + warp * chunk);
-  const int v_end = min(p_end, v_begin + chunk);
-  const size_t row = static_cast<size_t>(b) * V;
-  int* my = cnt + warp * S;
-
-  for (int vb = v_begin; vb < v_end; vb += 32) {
-    const int v = vb + lane;
-    int key = -1;
-    if (v < v_end) {
-      const float sc = ldg_f32<T>(reps + row + v);
-      const int s = __ldg(idx + row + v);
-      if (sc > 0.f && s >= 0 && s < S) key = s;
-    }
-    const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
-    if (key >= 0 && lane == __ffs(peers) - 1) my[key] += __popc(peers);
-  }
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i)
+    if (key[i] >= 0) atomicAdd(&hist[key[i]], 1);
   __syncthreads();
+  int* out = cnt + (static_cast<size_t>(b) * n_chunks + c) * S;
+  for (int i = threadIdx.x; i < S; i += blockDim.x) out[i] = hist[i];
+}
 
-  // This CTA's column sums; each thread owns a contiguous range of positions.
-  const int per = (S + blockDim.x - 1) / blockDim.x;
-  const int k_begin = min(S, static_cast<int>(threadIdx.x) * per), k_end = min(S, k_begin + per);
-  for (int k = k_begin; k < k_end; ++k) {
-    int run = 0;
-    for (int w = 0; w < nw; ++w) {
-      const int x = cnt[w * S + k];
-      cnt[w * S + k] = run;
-      run += x;
-    }
-    tot[k] = run;
-  }
-  int local = 0;
-  if (P > 1) {
-    cluster.sync();  // every CTA's tot[] is complete
-    for (int k = k_begin; k < k_end; ++k) {
-      int before = 0, all = 0;
-      for (int r = 0; r < P; ++r) {
-        const int x = *cluster.map_shared_rank(tot + k, r);
-        before += r < c ? x : 0;
-        all += x;
-      }
-      base[k] = before;
-      full[k] = all;
-      local += all;
-    }
-    cluster.sync();  // no CTA reads another's tot[] past this point
-  } else {
-    for (int k = k_begin; k < k_end; ++k) local += tot[k];
-  }
-
-  // Exclusive scan over positions of the bucket sizes full[s].
-  int incl = local;
+// Block-wide exclusive scan of one int per thread (blockDim.x = 1024).
+__device__ __forceinline__ int block_exclusive_scan(int x, int* tmp /*[33]*/, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = x;
+#pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
     if (lane >= o) incl += y;
   }
-  if (lane == 31) scan_tmp[warp] = incl;
+  if (lane == 31) tmp[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    int t = lane < nw ? scan_tmp[lane] : 0;
+    int t = lane < static_cast<int>(blockDim.x >> 5) ? tmp[lane] : 0;
+#pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xFFFFFFFFu, t, o);
       if (lane >= o) t += y;
     }
-    if (lane < nw) scan_tmp[lane] = t;  // inclusive per-warp totals
-    if (lane == 31) scan_tmp[32] = t;
+    tmp[lane] = t;  // inclusive per-warp totals
   }
   __syncthreads();
-  int run = incl - local + (warp > 0 ? scan_tmp[warp - 1] : 0);
-  int* orow = offs + static_cast<size_t>(b) * (S + 1);
-  for (int k = k_begin; k < k_end; ++k) {
-    if (c == 0) orow[k] = run;
-    const int start = run + (P > 1 ? base[k] : 0);
-    for (int w = 0; w < nw; ++w) cnt[w * S + k] += start;
-    run += full[k];
-  }
-  if (c == 0 && threadIdx.x == 0) orow[S] = scan_tmp[32];
+  total = tmp[(blockDim.x >> 5) - 1];
+  const int r = incl - x + (warp > 0 ? tmp[warp - 1] : 0);
   __syncthreads();
+  return r;
+}
 
-  int2* erow = ent + row;
-  const unsigned lt = (1u << lane) - 1u;
-  for (int vb = v_begin; vb < v_end; vb += 32) {
-    const int v = vb + lane;
-    int key = -1;
-    float gp = 0.f;
-    if (v < v_end) {
-      const float sc = ldg_f32<T>(reps + row + v);
-      const int s = __ldg(idx + row + v);
-      if (sc > 0.f && s >= 0 && s < S) {
-        key = s;
-        gp = ldg_f32<T>(g + row + v) * expf(-sc);
+__global__ void __launch_bounds__(1024)
+    sort_scan_kernel(int S, int n_chunks, int* __restrict__ cnt, int* __restrict__ offs) {
+  __shared__ int tmp[33];
+  const int b = blockIdx.x;
+  int* crow = cnt + static_cast<size_t>(b) * n_chunks * S;
+  int* orow = offs + static_cast<size_t>(b) * (S + 1);
+  int carry = 0;
+  for (int s0 = 0; s0 < S; s0 += blockDim.x) {
+    const int s = s0 + static_cast<int>(threadIdx.x);
+    int run = 0;
+    if (s < S) {
+      // 16 chunks' counts loaded together, then turned into their prefix
+      for (int c0 = 0; c0 < n_chunks; c0 += 16) {
+        int x[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          x[j] = c0 + j < n_chunks ? __ldcg(crow + static_cast<size_t>(c0 + j) * S + s) : 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (c0 + j < n_chunks) crow[static_cast<size_t>(c0 + j) * S + s] = run;
+          run += x[j];
+        }
       }
     }
-    const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
-    int slot = 0;
-    if (key >= 0) slot = my[key] + __popc(peers & lt);
+    int total = 0;
+    const int ex = block_exclusive_scan(run, tmp, total);
+    if (s < S) orow[s] = carry + ex;
+    carry += total;
+  }
+  if (threadIdx.x == 0) orow[S] = carry;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    sort_scatter_kernel(const T* __restrict__ g, const T* __restrict__ reps,
+                        const int32_t* __restrict__ idx, int S, int V, int chunk, int n_chunks,
+                        const int* __restrict__ cnt, const int* __restrict__ offs,
+                        int2* __restrict__ ent) {
+  extern __shared__ int sbase[];  // [S] bucket base of this chunk, then [nw][S] 16-bit counters
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int nw = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint16_t* wcnt = reinterpret_cast<uint16_t*>(sbase + S);
+  const size_t row = static_cast<size_t>(b) * V;
+  const int c_end = min(V, (c + 1) * chunk);
+  const int v_begin = min(c_end, c * chunk + warp * kSortWarpIds);
+  const int v_end = min(c_end, v_begin + kSortWarpIds);
+  int key[kSortIters];
+  float sc[kSortIters], gv[kSortIters];
+  sort_load_keys<T>(reps, idx, row, v_begin, v_end, S, lane, key, sc);
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i) {
+    const int v = v_begin + 32 * i + lane;
+    gv[i] = key[i] >= 0 ? ldg_f32<T>(g + row + v) : 0.f;
+  }
+  const int* obase = offs + static_cast<size_t>(b) * (S + 1);
+  const int* cbase = cnt + (static_cast<size_t>(b) * n_chunks + c) * S;
+  for (int i = threadIdx.x; i < S; i += blockDim.x) sbase[i] = __ldg(obase + i) + __ldg(cbase + i);
+  for (int i = threadIdx.x; i < nw * S; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  uint16_t* my = wcnt + warp * S;
+  unsigned peers[kSortIters];
+  const int nbits = key_bits(S);
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i) {
+    peers[i] = same_key_lanes(key[i], nbits);
+    if (key[i] >= 0 && lane == __ffs(peers[i]) - 1)
+      my[key[i]] = static_cast<uint16_t>(my[key[i]] + __popc(peers[i]));
     __syncwarp();
-    if (key >= 0) {
-      erow[slot] = make_int2(v, __float_as_int(gp));
-      if (lane == __ffs(peers) - 1) my[key] += __popc(peers);
+  }
+  __syncthreads();
+  // per position: exclusive prefix over the warps of this CTA (in place)
+  for (int s = threadIdx.x; s < S; s += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < nw; ++w) {
+      const int x = wcnt[w * S + s];
+      wcnt[w * S + s] = static_cast<uint16_t>(run);
+      run += x;
+    }
+  }
+  __syncthreads();
+  int2* erow = ent + row;
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int i = 0; i < kSortIters; ++i) {
+    const int k = key[i];
+    int slot = 0;
+    if (k >= 0) slot = sbase[k] + my[k] + __popc(peers[i] & lt);
+    __syncwarp();
+    if (k >= 0) {
+      const float gp = gv[i] * expf(-sc[i]);
+      erow[slot] = make_int2(v_begin + 32 * i + lane, __float_as_int(gp));
+      if (lane == __ffs(peers[i]) - 1) my[k] = static_cast<uint16_t>(my[k] + __popc(peers[i]));
     }
     __syncwarp();
   }
@@ -579,58 +649,42 @@ int set_smem(K kernel, int bytes, const char* what) {
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, what);
 }
 
-// Cluster size P for the sort: enough CTAs for two per SM (1, 2, 4 or 8 per
-// batch row). Shared memory per CTA: nw warp rows of S counters plus one (P = 1)
-// or three (P > 1) rows, 224 KB at most; long rows that leave fewer than 8
-// warps with P > 1 take P = 1.
-constexpr int kSortSmemInts = 56 * 1024;
-constexpr int kSortMaxS = kSortSmemInts / 2;
-
+// The sort's three launches (K2 above). Shared memory: S ints of histogram
+// (count); S ints of bucket bases and nw x S 16-bit counters (scatter).
 template <typename T>
 int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int B, int S, int V,
                 const BwdWorkspace& ws, cudaStream_t stream) {
   if (S > kSortMaxS)
     return fail(SPARTON_ERR_UNSUPPORTED, "backward supports S <= %d (got %d)", kSortMaxS, S);
-  int P = 1;
-  while (P < 8 && static_cast<long long>(B) * P < 2ll * device_sm_count()) P *= 2;
-  if (P > 1 && kSortSmemInts / S - 3 < 8) P = 1;
-  int nw = kSortSmemInts / S - (P > 1 ? 3 : 1);
-  if (nw > 32) nw = 32;
-  const size_t smem = static_cast<size_t>(nw + (P > 1 ? 3 : 1)) * S * sizeof(int);
-  if (smem > 48 * 1024) {
-    const int st = set_smem(bwd_sort_kernel<T>, static_cast<int>(smem),
-                            "cudaFuncSetAttribute(bwd_sort_kernel)");
-    if (st != SPARTON_OK) return st;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(P), static_cast<unsigned>(B));
-  cfg.blockDim = dim3(static_cast<unsigned>(nw * 32));
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(P);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (P > 1 && !cluster_fits(bwd_sort_kernel<T>, &cfg, P, smem)) {
-    // A cluster that cannot be co-scheduled (shared memory, partitioned GPU)
-    // falls back to one CTA per batch row.
-    {
-      P = 1;
-      nw = kSortSmemInts / S - 1;
-      if (nw > 32) nw = 32;
-      cfg.gridDim = dim3(1u, static_cast<unsigned>(B));
-      cfg.blockDim = dim3(static_cast<unsigned>(nw * 32));
-      cfg.dynamicSmemBytes = static_cast<size_t>(nw + 1) * S * sizeof(int);
-      attr[0].val.clusterDim.x = 1;
-    }
-  }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, bwd_sort_kernel<T>, static_cast<const T*>(grad_reps),
-                                           static_cast<const T*>(reps), idx, S, V, ws.offs, ws.ent,
-                                           ws.status, ws.row_counter);
-  if (e != cudaSuccess) return cuda_fail(e, "bwd_sort_kernel launch");
+  const int nw = sort_warps(S);
+  const int chunk = nw * kSortWarpIds;
+  const int n_chunks = (V + chunk - 1) / chunk;
+  const size_t smem_count = static_cast<size_t>(S) * sizeof(int);
+  const size_t smem_scatter = static_cast<size_t>(S) * (sizeof(int) + nw * sizeof(uint16_t));
+  int st = SPARTON_OK;
+  if (smem_count > 48 * 1024)
+    st = set_smem(sort_count_kernel<T>, static_cast<int>(smem_count),
+                  "cudaFuncSetAttribute(sort_count_kernel)");
+  if (st == SPARTON_OK && smem_scatter > 48 * 1024)
+    st = set_smem(sort_scatter_kernel<T>, static_cast<int>(smem_scatter),
+                  "cudaFuncSetAttribute(sort_scatter_kernel)");
+  if (st != SPARTON_OK) return st;
+  const dim3 grid(static_cast<unsigned>(n_chunks), static_cast<unsigned>(B));
+  sort_count_kernel<T><<<grid, static_cast<unsigned>(nw * 32), smem_count, stream>>>(static_cast<const T*>(reps), idx, S, V,
+                                                          chunk, n_chunks, ws.sort_cnt,
+                                                          ws.status, ws.row_counter);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sort_count_kernel launch");
+  const unsigned scan_threads = static_cast<unsigned>(S >= 1024 ? 1024 : (S + 31) / 32 * 32);
+  sort_scan_kernel<<<static_cast<unsigned>(B), scan_threads, 0, stream>>>(S, n_chunks,
+                                                                          ws.sort_cnt, ws.offs);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sort_scan_kernel launch");
+  sort_scatter_kernel<T><<<grid, static_cast<unsigned>(nw * 32), smem_scatter, stream>>>(
+      static_cast<const T*>(grad_reps), static_cast<const T*>(reps), idx, S, V, chunk, n_chunks,
+      ws.sort_cnt, ws.offs, ws.ent);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sort_scatter_kernel launch");
   return SPARTON_OK;
 }
 

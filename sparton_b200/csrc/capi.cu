@@ -227,6 +227,53 @@ int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx, con
                     d_weight, d_bias, d_hidden_dtype, d_param_dtype, ws, st);
 }
 
+size_t sparton_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0 || M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return 0;
+  return gemm_workspace_bytes(M, N, K);
+}
+
+int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const void* bias,
+                 int dtype, int64_t M, int64_t N, int64_t K, void* C, int c_dtype, int64_t ldc,
+                 void* workspace, size_t workspace_size, void* stream) {
+  if (dtype != SPARTON_DTYPE_BF16 && dtype != SPARTON_DTYPE_F16)
+    return fail(SPARTON_ERR_UNSUPPORTED, "sparton_gemm takes bf16 or f16 operands (dtype %d)",
+                dtype);
+  if (c_dtype != dtype && c_dtype != SPARTON_DTYPE_F32)
+    return fail(SPARTON_ERR_UNSUPPORTED, "c_dtype must equal dtype or be F32");
+  if ((a_layout != SPARTON_LAYOUT_ROWS && a_layout != SPARTON_LAYOUT_COLS) ||
+      (b_layout != SPARTON_LAYOUT_ROWS && b_layout != SPARTON_LAYOUT_COLS))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "unknown operand layout");
+  if (M < 0 || N < 0 || K < 0 || M > (1 << 30) || N > (1 << 30) || K > (1 << 30))
+    return fail(SPARTON_ERR_UNSUPPORTED, "sizes out of range (M=%lld N=%lld K=%lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (ldc < N) return fail(SPARTON_ERR_INVALID_ARGUMENT, "ldc=%lld < N=%lld", (long long)ldc,
+                           (long long)N);
+  // TMA: every row of an operand starts on a 16-byte boundary.
+  const int64_t a_inner = a_layout == SPARTON_LAYOUT_ROWS ? K : M;
+  const int64_t b_inner = b_layout == SPARTON_LAYOUT_ROWS ? K : N;
+  if (a_inner % 8 != 0 || b_inner % 8 != 0)
+    return fail(SPARTON_ERR_UNSUPPORTED,
+                "the contiguous dimension of each operand must be a multiple of 8 (A: %lld, B: "
+                "%lld)",
+                (long long)a_inner, (long long)b_inner);
+  SPARTON_TRY(check_workspace(workspace, workspace_size, gemm_workspace_bytes(M, N, K)));
+  if (M == 0 || N == 0) return SPARTON_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "A / B / C is NULL");
+  if (!aligned(A, 16) || !aligned(B, 16))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "A and B must be 16-byte aligned");
+  SPARTON_TRY(check_device());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    // Empty contraction: C = bias broadcast (or 0); written by the reduction-free
+    // path with no operand reads.
+    return fail(SPARTON_ERR_UNSUPPORTED, "K == 0 is not supported");
+  }
+  return launch_gemm(dtype, c_dtype, a_layout == SPARTON_LAYOUT_COLS,
+                     b_layout == SPARTON_LAYOUT_COLS, A, B, bias, static_cast<int>(M),
+                     static_cast<int>(N), static_cast<int>(K), C, ldc, workspace, st);
+}
+
 int sparton_read_device_status(const void* workspace, void* stream, uint32_t* code) {
   if (workspace == nullptr || code == nullptr)
     return fail(SPARTON_ERR_INVALID_ARGUMENT, "workspace / code is NULL");

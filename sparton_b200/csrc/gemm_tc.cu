@@ -1,0 +1,509 @@
+// gemm_tc.cu — a plain tcgen05 GEMM for the contractions around the head:
+//   C[M,N] = sum_k A[m,k] * B[n,k]  (+ bias[n]),  16-bit inputs, fp32 sums.
+//
+// Upstream computes these with torch (cuBLAS) calls: the dense layer of the MLM
+// transform in front of the head and its two backward products
+// (hhkbble/sparton training/model.py:25-35: RobertaTransform.dense, BERT's
+// predictions.transform.dense, used at :82-85), and the InfoNCE scores
+// q_reps @ d_reps.T with their backward (training/train.py:73-77). Here they run
+// on the same machinery as the head's forward kernel (fwd_tc.cu): TMA tiles into
+// a 4-stage mbarrier ring, one elected thread issuing tcgen05.mma kind::f16 into
+// double-buffered TMEM accumulators, four epilogue warps reading TMEM.
+//
+// Operand layouts. Each operand is dense row-major in memory in one of two ways:
+//   "rows" (K-major): A as [M][K], B as [N][K]: the contraction index is
+//                     contiguous, as for y = x @ W.T with x [M,K], W [N,K];
+//   "cols" (MN-major): A as [K][M], B as [K][N]: the output index is
+//                     contiguous, as for dx = dy @ W (B = W [K=N_out][N=K_in])
+//                     or dW = dy.T @ x (A = dy [K][M], B = x [K][N]).
+// TMA loads either form with 128-byte swizzle: a K-major tile is one box of
+// [rows x 64 k]; an MN-major tile is boxes of [64 rows (contiguous) x 64 k]
+// placed 8 KB apart, which is the canonical MN-major layout the tcgen05 shared
+// memory descriptor describes with leading byte offset 8 KB (between 64-element
+// MN blocks) and stride byte offset 1 KB (between groups of 8 k).
+//
+// Work units are (output tile of 128 x 256, split of the K range). With one
+// split the epilogue adds the bias and stores C in its dtype; with several
+// (few output tiles, long K: the InfoNCE scores, the dense weight's gradient)
+// every split stores its fp32 partial tile into the workspace and
+// gemm_reduce_kernel adds the splits in a fixed order (deterministic), adds
+// the bias and stores C. The split count depends only on the shape.
+//
+// Every wait is bounded (ptx.cuh); a CTA that gives up records a status code in
+// the workspace header, drains its copies and MMAs, frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "dtype.cuh"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sparton {
+namespace {
+
+constexpr int kBM = 128;   // output rows per tile = MMA M = TMEM lanes
+constexpr int kBN = 256;   // output columns per tile = max MMA N
+constexpr int kBK = 64;    // k per stage: 128-byte rows
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kBBytes = kBN * kBK * 2;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kBoxBytes = 64 * kBK * 2;  // one MN-major box: 64 rows x 64 k
+constexpr int kNumAcc = 2;
+constexpr int kTmemCols = kNumAcc * kBN;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+
+constexpr int kBarFull = 0;
+constexpr int kBarEmpty = kBarFull + kStages;
+constexpr int kBarTFull = kBarEmpty + kStages;
+constexpr int kBarTEmpty = kBarTFull + kNumAcc;
+constexpr int kBarDrain = kBarTEmpty + kNumAcc;
+constexpr int kNumBars = kBarDrain + 1;
+constexpr int kCtrlOffset = kStages * kStageBytes;
+constexpr int kTmemHolderOffset = kCtrlOffset + kNumBars * 8;
+constexpr int kAbortOffset = kTmemHolderOffset + 4;
+constexpr int kCtrlBytes = 256;
+constexpr int kSmemBytes = kCtrlOffset + kCtrlBytes + 1024;
+
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks, splits, kb_per_split;
+  long long units;
+  const void* bias;   // [N] in the output's element type family (T), or NULL
+  void* C;            // [M][ldc] of type O (splits == 1)
+  long long ldc;
+  float* partial;     // [splits][M][N] fp32 (splits > 1)
+  bool vec_store;     // rows of C start on 16-byte boundaries
+  unsigned int* status;
+};
+
+struct Ctrl {
+  uint32_t bar0;
+  volatile int* abort_flag;
+  __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * i; }
+};
+
+struct UnitPos {
+  int m0, n0, kb0, kb1, split;
+};
+
+__device__ __forceinline__ UnitPos unit_pos(const GemmParams& p, long long u) {
+  const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  UnitPos o;
+  o.split = static_cast<int>(u / tiles);
+  const int t = static_cast<int>(u - static_cast<long long>(o.split) * tiles);
+  o.m0 = (t / p.n_tiles) * kBM;
+  o.n0 = (t % p.n_tiles) * kBN;
+  o.kb0 = o.split * p.kb_per_split;
+  o.kb1 = min(p.k_blocks, o.kb0 + p.kb_per_split);
+  return o;
+}
+
+// Loads the A (kAmn: MN-major) and B (kBmn) tiles of k block kb into a stage.
+template <bool kAmn, bool kBmn>
+__device__ __forceinline__ void load_stage(const CUtensorMap* tmA, const CUtensorMap* tmB,
+                                           uint32_t a_dst, uint32_t full, const UnitPos& u,
+                                           int kb) {
+  const int k0 = kb * kBK;
+  if (kAmn) {
+#pragma unroll
+    for (int i = 0; i < kBM / 64; ++i) tma_load_2d(a_dst + i * kBoxBytes, tmA, full, u.m0 + 64 * i, k0);
+  } else {
+    tma_load_2d(a_dst, tmA, full, k0, u.m0);
+  }
+  const uint32_t b_dst = a_dst + kABytes;
+  if (kBmn) {
+#pragma unroll
+    for (int i = 0; i < kBN / 64; ++i) tma_load_2d(b_dst + i * kBoxBytes, tmB, full, u.n0 + 64 * i, k0);
+  } else {
+    tma_load_2d(b_dst, tmB, full, k0, u.n0);
+  }
+}
+
+template <bool kAmn, bool kBmn>
+__device__ void run_producer(const GemmParams& p, const CUtensorMap* tmA, const CUtensorMap* tmB,
+                             uint32_t stage_base, const Ctrl& c) {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t issued_mask = 0, issued_parity = 0;
+  bool ok = true;
+  for (long long u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    const UnitPos up = unit_pos(p, u);
+    for (int kb = up.kb0; kb < up.kb1; ++kb) {
+      if (!mbar_wait_bounded_warp(c.bar(kBarEmpty + stage), phase ^ 1, c.abort_flag, p.status,
+                                  SPARTON_DEV_TIMEOUT_PRODUCER)) {
+        ok = false;
+        break;
+      }
+      if (elect_one()) {
+        const uint32_t full = c.bar(kBarFull + stage);
+        mbar_arrive_expect_tx(full, kStageBytes);  // out-of-range parts are zero-filled
+        load_stage<kAmn, kBmn>(tmA, tmB, stage_base + stage * kStageBytes, full, up, kb);
+      }
+      __syncwarp();
+      issued_mask |= 1u << stage;
+      issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  for (int s = 0; s < kStages; ++s) {
+    if (!(issued_mask & (1u << s))) continue;
+    const uint32_t par = (issued_parity >> s) & 1;
+    const uint32_t bar = c.bar((ok ? kBarEmpty : kBarFull) + s);
+    if (!mbar_wait_drain(bar, par)) atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
+  }
+}
+
+// Shared-memory descriptor of one MMA's operand slice (16 k) at k step kk.
+template <bool kMn>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+  if (!kMn) return umma_desc_k_sw128(base + kk * 32);
+  // MN-major, 128-byte swizzle: 8-row k groups 1 KB apart (stride byte offset),
+  // 64-element MN blocks kBoxBytes apart (leading byte offset); 16 k = 2 KB.
+  uint64_t d = umma_desc_k_sw128(base + kk * 2048);
+  d &= ~(static_cast<uint64_t>(0x3FFFu) << 16);
+  d |= static_cast<uint64_t>(kBoxBytes >> 4) << 16;
+  return d;
+}
+
+template <uint32_t kFmt, bool kAmn, bool kBmn>
+__device__ void run_mma(const GemmParams& p, uint32_t stage_base, uint32_t tmem_base,
+                        const Ctrl& c) {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t tile = 0;
+  bool ok = true, issued = false;
+  for (long long u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    const UnitPos up = unit_pos(p, u);
+    const int acc = tile % kNumAcc;
+    const uint32_t aph = (tile / kNumAcc) & 1;
+    if (!mbar_wait_bounded_warp(c.bar(kBarTEmpty + acc), aph ^ 1, c.abort_flag, p.status,
+                                SPARTON_DEV_TIMEOUT_MMA)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after_sync();
+    const uint32_t n_mma = static_cast<uint32_t>(min(kBN, (p.N - up.n0 + 15) / 16 * 16));
+    const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma) | (kAmn ? (1u << 15) : 0u) |
+                           (kBmn ? (1u << 16) : 0u);
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+    for (int kb = up.kb0; kb < up.kb1; ++kb) {
+      if (!mbar_wait_bounded_warp(c.bar(kBarFull + stage), phase, c.abort_flag, p.status,
+                                  SPARTON_DEV_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      if (elect_one()) {
+        const uint32_t a_addr = stage_base + stage * kStageBytes;
+        const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16(d_tmem, operand_desc<kAmn>(a_addr, kk), operand_desc<kBmn>(b_addr, kk), idesc,
+                   (kb > up.kb0 || kk > 0) ? 1u : 0u);
+        umma_commit(c.bar(kBarEmpty + stage));
+      }
+      __syncwarp();
+      issued = true;
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+    if (elect_one()) umma_commit(c.bar(kBarTFull + acc));
+    __syncwarp();
+    ++tile;
+  }
+  if (!ok && issued) {
+    if (elect_one()) umma_commit(c.bar(kBarDrain));
+    __syncwarp();
+    if (!mbar_wait_drain(c.bar(kBarDrain), 0)) atomicCAS(p.status, 0u, SPARTON_DEV_TIMEOUT_DRAIN);
+  }
+}
+
+// Stores 32 consecutive outputs of row m starting at column n (n < N).
+template <typename O>
+__device__ __forceinline__ void store_row_chunk(const GemmParams& p, int m, int n,
+                                                const float (&v)[32]) {
+  O* dst = static_cast<O*>(p.C) + static_cast<size_t>(m) * p.ldc + n;
+  const int cnt = min(32, p.N - n);
+  if (p.vec_store && cnt == 32) {
+    constexpr int kPer = 16 / sizeof(O);
+#pragma unroll
+    for (int i = 0; i < 32; i += kPer) {
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+      if constexpr (sizeof(O) == 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wp[j] = __float_as_uint(v[i + j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wp[j] = pack2<O>(v[i + 2 * j], v[i + 2 * j + 1]);
+      }
+      *reinterpret_cast<uint4*>(dst + i) = w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < cnt) dst[i] = from_f32<O>(v[i]);
+  }
+}
+
+template <typename T, typename O>
+__device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
+                             int lane) {
+  const int quad = warp & 3;
+  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+  uint32_t tile = 0;
+  for (long long u = blockIdx.x; u < p.units; u += gridDim.x) {
+    const UnitPos up = unit_pos(p, u);
+    const int acc = tile % kNumAcc;
+    const uint32_t aph = (tile / kNumAcc) & 1;
+    const bool got = mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
+                                       SPARTON_DEV_TIMEOUT_EPILOGUE);
+    if (!__all_sync(0xFFFFFFFFu, got)) break;
+    tc_fence_after_sync();
+    const int m = up.m0 + quad * 32 + lane;
+    const int nch = (min(kBN, p.N - up.n0) + 31) >> 5;
+    for (int ch = 0; ch < nch; ++ch) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(lane_base + static_cast<uint32_t>(acc * kBN + 32 * ch), r);
+      tmem_ld_wait(r);
+      const int n = up.n0 + 32 * ch;
+      if (m >= p.M) continue;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (p.splits > 1) {
+        float* dst = p.partial + (static_cast<size_t>(up.split) * p.M + m) * p.N + n;
+        const int cnt = min(32, p.N - n);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < cnt) dst[i] = v[i];
+      } else {
+        if (p.bias != nullptr) {
+          const T* bp = static_cast<const T*>(p.bias) + n;
+          const int cnt = min(32, p.N - n);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < cnt) v[i] += to_f32<T>(bp[i]);
+        }
+        store_row_chunk<O>(p, m, n, v);
+      }
+    }
+    tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(c.bar(kBarTEmpty + acc));
+    ++tile;
+  }
+}
+
+template <typename T, typename O, uint32_t kFmt, bool kAmn, bool kBmn>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t stage_base = smem_addr(smem);
+  Ctrl c;
+  c.bar0 = stage_base + kCtrlOffset;
+  c.abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOffset);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kTmemHolderOffset);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(c.bar(kBarFull + s), 1);
+      mbar_init(c.bar(kBarEmpty + s), 1);
+    }
+    for (int a = 0; a < kNumAcc; ++a) {
+      mbar_init(c.bar(kBarTFull + a), 1);
+      mbar_init(c.bar(kBarTEmpty + a), kEpiWarps);
+    }
+    mbar_init(c.bar(kBarDrain), 1);
+    *c.abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_holder;
+  if (warp == 0) {
+    run_producer<kAmn, kBmn>(p, &tmA, &tmB, stage_base, c);
+    __syncwarp();
+  } else if (warp == 1) {
+    run_mma<kFmt, kAmn, kBmn>(p, stage_base, tmem_base, c);
+    __syncwarp();
+  } else {
+    run_epilogue<T, O>(p, tmem_base, c, warp, lane);
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// C[m, n] = sum over splits (in order) of partial[s][m][n] (+ bias[n]).
+template <typename T, typename O>
+__global__ void __launch_bounds__(256) gemm_reduce_kernel(const float* __restrict__ partial,
+                                                          int splits, int M, int N,
+                                                          const T* __restrict__ bias, O* C,
+                                                          long long ldc) {
+  const long long total = static_cast<long long>(M) * N;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += 256ll * gridDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += __ldcs(partial + k * total + i);
+    const int m = static_cast<int>(i / N), n = static_cast<int>(i - static_cast<long long>(m) * N);
+    if (bias != nullptr) s += to_f32<T>(bias[n]);
+    C[static_cast<size_t>(m) * ldc + n] = from_f32<O>(s);
+  }
+}
+
+// ----------------------------------------------------------------------- host
+// Splits of the K range: enough units for about two per SM when the output has
+// few tiles, each split at least 4 k blocks; a function of the shape only.
+constexpr long long kTargetUnits = 296;
+
+void plan(int M, int N, int K, int& m_tiles, int& n_tiles, int& k_blocks, int& splits,
+          int& kb_per) {
+  m_tiles = (M + kBM - 1) / kBM;
+  n_tiles = (N + kBN - 1) / kBN;
+  k_blocks = (K + kBK - 1) / kBK;
+  const long long tiles = static_cast<long long>(m_tiles) * n_tiles;
+  long long s = 1;
+  if (tiles < kTargetUnits / 2 && k_blocks >= 8) {
+    s = (kTargetUnits + tiles - 1) / tiles;
+    s = s < k_blocks / 4 ? s : k_blocks / 4;
+    if (s < 1) s = 1;
+  }
+  kb_per = static_cast<int>((k_blocks + s - 1) / s);
+  splits = (k_blocks + kb_per - 1) / kb_per;  // every split has >= 1 k block
+}
+
+int make_operand_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, bool mn_major,
+                     int mn, int K, int box_rows) {
+  // K-major: [mn][K], box [box_rows x 64 k]; MN-major: [K][mn], box [64 k x 64 mn].
+  if (mn_major)
+    return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(mn), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(mn) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(K), static_cast<uint64_t>(mn),
+                            static_cast<uint64_t>(K) * 2, kBK, static_cast<uint32_t>(box_rows),
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename T, typename O, uint32_t kFmt, bool kAmn, bool kBmn>
+int launch_typed(CUtensorMapDataType dt, const void* A, const void* B, const void* bias, int M,
+                 int N, int K, void* C, long long ldc, void* workspace, cudaStream_t stream) {
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  plan(M, N, K, p.m_tiles, p.n_tiles, p.k_blocks, p.splits, p.kb_per_split);
+  p.units = static_cast<long long>(p.m_tiles) * p.n_tiles * p.splits;
+  p.bias = bias;
+  p.C = C;
+  p.ldc = ldc;
+  p.status = static_cast<unsigned int*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  p.vec_store = (reinterpret_cast<uintptr_t>(C) % 16 == 0) && ((ldc * sizeof(O)) % 16 == 0);
+  CUtensorMap tmA, tmB;
+  int st = make_operand_map(&tmA, dt, A, kAmn, M, K, kBM);
+  if (st != SPARTON_OK) return st;
+  st = make_operand_map(&tmB, dt, B, kBmn, N, K, kBN);
+  if (st != SPARTON_OK) return st;
+
+  static std::mutex mu;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !attr_done[dev]) {
+      e = cudaFuncSetAttribute(gemm_tc_kernel<T, O, kFmt, kAmn, kBmn>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_tc_kernel)");
+      attr_done[dev] = true;
+    }
+  }
+  e = cudaMemsetAsync(workspace, 0, 256, stream);  // status word
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  const long long sms = device_sm_count();
+  const unsigned grid = static_cast<unsigned>(p.units < sms ? p.units : sms);
+  gemm_tc_kernel<T, O, kFmt, kAmn, kBmn><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_tc_kernel launch");
+  if (p.splits > 1) {
+    const long long total = static_cast<long long>(M) * N;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 4 * sms) blocks = 4 * sms;
+    gemm_reduce_kernel<T, O><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        p.partial, p.splits, M, N, static_cast<const T*>(bias), static_cast<O*>(C), ldc);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_reduce_kernel launch");
+  }
+  return SPARTON_OK;
+}
+
+template <typename T, uint32_t kFmt, bool kAmn, bool kBmn>
+int launch_out(CUtensorMapDataType dt, int c_dtype, const void* A, const void* B,
+               const void* bias, int M, int N, int K, void* C, long long ldc, void* ws,
+               cudaStream_t s) {
+  if (c_dtype == SPARTON_DTYPE_F32)
+    return launch_typed<T, float, kFmt, kAmn, kBmn>(dt, A, B, bias, M, N, K, C, ldc, ws, s);
+  return launch_typed<T, T, kFmt, kAmn, kBmn>(dt, A, B, bias, M, N, K, C, ldc, ws, s);
+}
+
+template <typename T, uint32_t kFmt>
+int launch_layouts(CUtensorMapDataType dt, int c_dtype, bool a_mn, bool b_mn, const void* A,
+                   const void* B, const void* bias, int M, int N, int K, void* C, long long ldc,
+                   void* ws, cudaStream_t s) {
+  if (!a_mn && !b_mn)
+    return launch_out<T, kFmt, false, false>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
+  if (!a_mn && b_mn)
+    return launch_out<T, kFmt, false, true>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
+  if (a_mn && !b_mn)
+    return launch_out<T, kFmt, true, false>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
+  return launch_out<T, kFmt, true, true>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
+}
+
+}  // namespace
+
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  int mt, nt, kb, splits, kbp;
+  plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), mt, nt, kb, splits, kbp);
+  return 256 + (splits > 1 ? static_cast<size_t>(splits) * M * N * 4 : 0);
+}
+
+int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, const void* B,
+                const void* bias, int M, int N, int K, void* C, long long ldc, void* workspace,
+                cudaStream_t stream) {
+  if (dtype == SPARTON_DTYPE_BF16)
+    return launch_layouts<__nv_bfloat16, 1u>(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c_dtype, a_mn, b_mn,
+                                             A, B, bias, M, N, K, C, ldc, workspace, stream);
+  if (dtype == SPARTON_DTYPE_F16)
+    return launch_layouts<__half, 0u>(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, c_dtype, a_mn, b_mn, A, B,
+                                      bias, M, N, K, C, ldc, workspace, stream);
+  return fail(SPARTON_ERR_UNSUPPORTED, "the tensor-core GEMM takes bf16 or f16 operands");
+}
+
+}  // namespace sparton

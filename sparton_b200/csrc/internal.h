@@ -115,17 +115,35 @@ inline FwdWorkspace fwd_workspace_carve(void* ws, int64_t B, int64_t S) {
 // gperm        B x V float       g' of those entries, same order
 // wrow         V x B int32       per vocab id: hidden row b*S + idx[b,v] of every b
 // wcoef        V x B float       per vocab id: g' of every b (0 when reps is 0)
+// sort_cnt     B x chunks x S int32  per (row, chunk of vocab ids, position):
+//              entries, then their prefix over the chunks (the sort's scratch;
+//              chunks = ceil(V / bwd_sort_chunk(S)))
 struct BwdWorkspace {
   unsigned int* status;
   unsigned int* row_counter;
   int* offs;
   int2* ent;   // [B][V] (v, bits of g') in CSR order by argmax position
   int2* went;  // [V][B] (b*S + idx[b,v], bits of g'), vocab-major
+  int* sort_cnt;
 };
+
+// Vocab ids per chunk of the backward's sort: 128 per warp, 8 warps unless
+// S 16-bit counters per warp plus S int32 bucket bases would exceed 220 KB of
+// shared memory (bwd.cu sort_warps).
+inline int64_t bwd_sort_chunk(int64_t S) {
+  int64_t nw = 8;
+  while (nw > 1 && (nw * 2 + 4) * S > 220 * 1024) nw >>= 1;
+  return nw * 128;
+}
+
+inline size_t bwd_sort_cnt_bytes(int64_t B, int64_t S, int64_t V) {
+  const int64_t chunks = (V + bwd_sort_chunk(S) - 1) / bwd_sort_chunk(S);
+  return align256(static_cast<size_t>(B * chunks * S) * 4);
+}
 
 inline size_t bwd_workspace_bytes(int64_t B, int64_t S, int64_t V) {
   return 256 + align256(static_cast<size_t>(B * (S + 1)) * 4) +
-         2 * align256(static_cast<size_t>(B * V) * 8);
+         2 * align256(static_cast<size_t>(B * V) * 8) + bwd_sort_cnt_bytes(B, S, V);
 }
 
 inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t V) {
@@ -139,6 +157,8 @@ inline BwdWorkspace bwd_workspace_carve(void* ws, int64_t B, int64_t S, int64_t 
   w.ent = reinterpret_cast<int2*>(base + off);
   off += align256(static_cast<size_t>(B * V) * 8);
   w.went = reinterpret_cast<int2*>(base + off);
+  off += align256(static_cast<size_t>(B * V) * 8);
+  w.sort_cnt = reinterpret_cast<int*>(base + off);
   return w;
 }
 
@@ -217,6 +237,15 @@ int launch_transform_bwd(int dtype, const void* dh, const void* y, const void* g
                          const float* mean, const float* rstd, int rows, int D, void* dy,
                          void* d_gamma, void* d_beta, void* d_bias, void* workspace,
                          cudaStream_t stream);
+
+// Plain tensor-core GEMM (gemm_tc.cu): C[M,N] = sum_k A[m,k] B[n,k] (+ bias[n]);
+// a_mn / b_mn: the operand is stored MN-major ([K][M] / [K][N]) instead of
+// K-major ([M][K] / [N][K]). dtype: bf16 / f16 operands (and bias); c_dtype:
+// dtype or F32. The workspace holds a 256-byte header and the split partials.
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, const void* B,
+                const void* bias, int M, int N, int K, void* C, long long ldc, void* workspace,
+                cudaStream_t stream);
 
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,

@@ -30,6 +30,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _lib
+from .gemm import gemm, pad_to, round_up
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -125,24 +126,49 @@ def flops_regularization(reps: torch.Tensor, *, process_group=None,
 
 
 class _Scores(torch.autograd.Function):
-    """q @ d.T in fp32, summed over the vocabulary shards of a process group."""
+    """q @ d.T in fp32, summed over the vocabulary shards of a process group.
+
+    16-bit reps on a GPU run on the library's tcgen05 GEMM: the forward as one
+    split-K contraction over the vocabulary with fp32 output, the backward as
+    gq = gs @ d and gd = gs.T @ q with gs rounded to the reps' dtype (what the
+    reference's bf16 matmul autograd computes, train.py:73-77), both reading d
+    and q in place through their transposed layout. The GEMM needs 16-byte
+    rows, so q and d are zero-padded once to a vocabulary multiple of 64 and
+    batch multiples of 8 (the padding adds zeros to every sum) and kept for the
+    backward."""
 
     @staticmethod
     def forward(ctx, q, d, group):
-        if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and d.dtype == q.dtype:
-            s = torch.mm(q, d.t(), out_dtype=torch.float32)  # 16-bit inputs, fp32 sums
+        Bq, V = q.shape
+        Bd = d.shape[0]
+        ctx.shapes = (Bq, Bd, V)
+        ctx.tc = q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and d.dtype == q.dtype
+        if ctx.tc:
+            Vp, Bq8, Bd8 = round_up(V, 64), round_up(Bq, 8), round_up(Bd, 8)
+            qp, dp = pad_to(q, Bq8, Vp), pad_to(d, Bd8, Vp)
+            s = gemm(qp, dp, out_dtype=torch.float32)[:Bq, :Bd]
+            ctx.save_for_backward(qp, dp)
         else:
             s = torch.matmul(q.float(), d.float().t())
+            ctx.save_for_backward(q, d)
+        s = s.contiguous()
         if group is not None:
             dist.all_reduce(s, op=dist.ReduceOp.SUM, group=group)
-        ctx.save_for_backward(q, d)
         return s
 
     @staticmethod
     def backward(ctx, gs):
-        q, d = ctx.saved_tensors
-        gq = (gs @ d.float()).to(q.dtype) if ctx.needs_input_grad[0] else None
-        gd = (gs.t() @ q.float()).to(d.dtype) if ctx.needs_input_grad[1] else None
+        Bq, Bd, V = ctx.shapes
+        need_q, need_d = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not ctx.tc:
+            q, d = ctx.saved_tensors
+            gq = (gs @ d.float()).to(q.dtype) if need_q else None
+            gd = (gs.t() @ q.float()).to(d.dtype) if need_d else None
+            return gq, gd, None
+        qp, dp = ctx.saved_tensors
+        gsp = pad_to(gs.to(qp.dtype), qp.shape[0], dp.shape[0])  # [Bq8, Bd8]
+        gq = gemm(gsp, dp, b_t=True)[:Bq, :V] if need_q else None        # gs @ d
+        gd = gemm(gsp, qp, a_t=True, b_t=True)[:Bd, :V] if need_d else None  # gs.T @ q
         return gq, gd, None
 
 
@@ -156,7 +182,13 @@ def scores(query_reps: torch.Tensor, doc_reps: torch.Tensor, *, process_group=No
 
 def info_nce_loss(query_reps: torch.Tensor, doc_reps: torch.Tensor, temperature: float = 1.0,
                   *, process_group=None) -> torch.Tensor:
-    """In-batch negatives contrastive loss (train.py:73-77)."""
+    """In-batch negatives contrastive loss (train.py:73-77). Query i's positive
+    is document i, so there must be at least as many documents as queries
+    (checked here; upstream's cross_entropy would fail on the device)."""
+    _require(query_reps.dim() == 2 and doc_reps.dim() == 2
+             and query_reps.shape[0] <= doc_reps.shape[0],
+             f"info_nce_loss needs at least as many documents as queries, got "
+             f"{tuple(query_reps.shape)} and {tuple(doc_reps.shape)}")
     s = scores(query_reps, doc_reps, process_group=process_group) / temperature
     labels = torch.arange(s.size(0), device=s.device)
     return F.cross_entropy(s, labels)

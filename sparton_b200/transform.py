@@ -31,6 +31,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
+from .gemm import gemm
 from .head import SpartonHead
 
 
@@ -89,10 +90,42 @@ def transform_bwd_impl(dh: torch.Tensor, y: torch.Tensor, gamma: torch.Tensor,
     return dy, dg, db, dbias
 
 
+def _tensor_core(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """16-bit operands with 16-byte rows: the dense layer and its backward
+    products run on the library's tcgen05 GEMM. fp32 keeps torch's fp32 GEMM
+    (tcgen05 has no fp32-exact kind; the fp32 path is held to rtol 1e-5)."""
+    return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype
+            and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
+
+
+def _dense_fwd(x, w, b):
+    """y = x @ w.T + b (nn.Linear), on the tensor-core GEMM when it applies."""
+    if not _tensor_core(x, w):
+        return F.linear(x, w, b)
+    lead = x.shape[:-1]
+    y = gemm(x.reshape(-1, x.shape[-1]), w, bias=b)
+    return y.reshape(*lead, w.shape[0])
+
+
+def _dense_bwd(dy, x, w, need_x: bool, need_w: bool):
+    """(dx = dy @ w, dw = dy.T @ x) of the dense layer; the GEMM reads dy, x
+    and w in place (w and, for dw, dy and x through their transposed layout)."""
+    D_in = x.shape[-1]
+    dy2 = dy.reshape(-1, dy.shape[-1])
+    x2 = x.reshape(-1, D_in)
+    if not _tensor_core(x, w):
+        dx = (dy @ w) if need_x else None
+        dw = (dy2.t() @ x2) if need_w else None
+        return dx, dw
+    dx = gemm(dy2, w, b_t=True).reshape(x.shape) if need_x else None
+    dw = gemm(dy2, x2, a_t=True, b_t=True, out_dtype=w.dtype) if need_w else None
+    return dx, dw
+
+
 class _Transform(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, dense_w, dense_b, gamma, beta, eps):
-        y = F.linear(x, dense_w, dense_b)  # plain GEMM (cuBLAS)
+        y = _dense_fwd(x, dense_w, dense_b)
         h, mean, rstd = transform_fwd_impl(y, gamma, beta, eps)
         ctx.save_for_backward(x, dense_w, y, gamma, mean, rstd)
         ctx.has_dense_bias = dense_b is not None
@@ -104,9 +137,7 @@ class _Transform(torch.autograd.Function):
         need = ctx.needs_input_grad
         dy, dg, db, dbias = transform_bwd_impl(dh, y, gamma, mean, rstd,
                                                need_params=any(need[2:5]))
-        D_in = x.shape[-1]
-        dx = (dy @ dense_w) if need[0] else None
-        dw = (dy.reshape(-1, dy.shape[-1]).t() @ x.reshape(-1, D_in)) if need[1] else None
+        dx, dw = _dense_bwd(dy, x, dense_w, need[0], need[1])
         return (dx, dw, dbias if (need[2] and ctx.has_dense_bias) else None,
                 dg if need[3] else None, db if need[4] else None, None)
 

@@ -85,18 +85,35 @@ def test_reg_capi_direct():
                                out.data_ptr(), ws.data_ptr(), 8, sh) == 3
 
 
+@pytest.mark.parametrize("shape", [(32, 32, 3000, 0.05), (21, 30, 2999, 0.05),
+                                   (128, 128, 30522, 100.0)],
+                         ids=lambda s: "Bq{}Bd{}V{}".format(*s[:3]))
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_info_nce_matches_oracle(dtype):
-    q = _reps(32, 3000, dtype, seed=1).cuda().requires_grad_(True)
-    d = _reps(32, 3000, dtype, seed=2).cuda().requires_grad_(True)
-    loss = losses.info_nce_loss(q, d, temperature=0.05)
+def test_info_nce_matches_oracle(dtype, shape):
+    """16-bit reps run on the tensor-core GEMM (zero-padded to 16-byte rows:
+    batch sizes not multiples of 8, an odd vocabulary); fp32 on torch. The
+    full-vocabulary case uses a temperature that keeps the logits O(1): its
+    scores (~1.7e4 from 30522 dense terms) carry fp32 rounding of ~1e-3, which
+    at temperature 0.05 alone would move the softmax gradients by more than
+    the tolerance."""
+    Bq, Bd, V, temp = shape
+    q = _reps(Bq, V, dtype, seed=1).cuda().requires_grad_(True)
+    d = _reps(Bd, V, dtype, seed=2).cuda().requires_grad_(True)
+    loss = losses.info_nce_loss(q, d, temperature=temp)
     loss.backward()
     want, dq, dd = lo.info_nce(q.detach().double().cpu().numpy(), d.detach().double().cpu().numpy(),
-                               0.05)
+                               temp)
     np.testing.assert_allclose(loss.item(), want, rtol=1e-4)
     r = max(RTOL[dtype], 1e-4)
     _close(q.grad, dq, r, "dq")
     _close(d.grad, dd, r, "dd")
+
+
+def test_info_nce_rejects_more_queries_than_documents():
+    q = _reps(30, 64, torch.bfloat16, seed=1).cuda()
+    d = _reps(21, 64, torch.bfloat16, seed=2).cuda()
+    with pytest.raises(ValueError):
+        losses.info_nce_loss(q, d)
 
 
 def test_losses_reject_cpu_tensors():
