@@ -584,6 +584,9 @@ def main(argv=None) -> int:
                     help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
                     help="stream priority of the NCCL process group (N > 1)")
+    ap.add_argument("--hidden-reduce", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: sum of the partial d_hidden over NVLink peer memory (packed "
+                         "rows only) or NCCL all-reduce of all rows in chunks")
     ap.add_argument("--legs", default="device,e2e,cpu,losses,sparse,transform",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
                          "(training losses on the head's output), sparse (CSR / top-k of "
@@ -651,6 +654,16 @@ def main(argv=None) -> int:
     dt = _lib.DTYPE[c["dtype"]]
     chunks = row_chunks(B, S * D * torch.empty((), dtype=dh_dtype).element_size())
     side = torch.cuda.Stream(dev)
+    peer = None
+    if world > 1 and args.hidden_reduce == "peer":
+        from sparton_b200.peer import PeerHiddenReduce
+
+        if not PeerHiddenReduce.usable(group, Hd):
+            raise RuntimeError("--hidden-reduce peer needs every rank on one node's GPUs (<= 8)")
+        peer = PeerHiddenReduce.get(group, dev, B * S, D, c["dtype"])
+    import sparton_b200.head as head_mod
+
+    head_mod.HIDDEN_REDUCE = args.hidden_reduce  # the e2e leg's SpartonHead does the same
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
     def step(k0=None, k1=None):
@@ -677,6 +690,23 @@ def main(argv=None) -> int:
                                        None, dW.data_ptr(), _lib.ptr(db),
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(),
                                        side.cuda_stream), "bwd dW")
+            stream.wait_stream(side)
+            return
+        if peer is not None:
+            # SpartonHead's sharded backward with the peer reduction: the fp32
+            # partial dH into this rank's peer buffer, then the sum of the
+            # packed rows over NVLink into dH while dW / db run on a side stream.
+            _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
+                                       Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs,
+                                       peer.partial(B, S).data_ptr(), None, None,
+                                       _lib.DTYPE[torch.float32], dt, wsb.data_ptr(),
+                                       wsb.numel(), sh), "bwd dH")
+            side.wait_stream(stream)
+            _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
+                                       Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs, None,
+                                       dW.data_ptr(), _lib.ptr(db), _lib.DTYPE[dh_dtype], dt,
+                                       wsb.data_ptr(), wsb.numel(), side.cuda_stream), "bwd dW")
+            peer.reduce(wsf, B, S, dH)
             stream.wait_stream(side)
             return
         # Sharded, with SpartonHead's sharded backward schedule: partial dH in
@@ -739,7 +769,13 @@ def main(argv=None) -> int:
     # mask_prepare + pack_prepare + forward; backward: sort, dH gather, dW list,
     # dW gather (db, when there is a bias, is summed inside the dW gather);
     # sharded, a sort and a dH gather per chunk of batch rows.
-    launches_per_step = 3 + (4 if world == 1 else 2 * len(chunks) + 2)
+    # sort: 3 kernels; dH and dW gathers; dW list; peer reduction: 4
+    if world == 1:
+        launches_per_step = 3 + 3 + 1 + 2
+    elif peer is not None:
+        launches_per_step = 3 + 3 + 1 + 2 + 4
+    else:
+        launches_per_step = 3 + len(chunks) * 4 + 2
 
     # ------------------------------------------------------------ inference forward
     # mask prepare + the forward without the argmax output (what SpartonHead
@@ -797,7 +833,9 @@ def main(argv=None) -> int:
         "config": {"workload": workload_desc(c),
                    "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
                    "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
-                   "dh_allreduce_chunks": len(chunks) if world > 1 else 0,
+                   "dh_reduce": (None if world == 1 else
+                                 "peer (NVLink loads, packed rows)" if peer is not None else
+                                 f"nccl all-reduce, {len(chunks)} chunks"),
                    "nccl_stream_priority": args.nccl_priority if world > 1 else None,
                    "l2": "flushed (256 MiB write) before every timed step"},
         "tokens_per_s": round(B * S / (step_ms * 1e-3), 1),

@@ -86,6 +86,7 @@ typedef enum {
 #define SPARTON_DEV_TIMEOUT_EPILOGUE 0x103u
 #define SPARTON_DEV_TIMEOUT_DRAIN 0x104u
 #define SPARTON_DEV_TIMEOUT_SELFTEST 0x1F0u /* sparton_selftest_wait_timeout only */
+#define SPARTON_DEV_TIMEOUT_PEER 0x105u     /* sparton_hidden_allreduce: a peer never signalled */
 
 int sparton_abi_version(void);
 
@@ -305,6 +306,42 @@ size_t sparton_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const void* bias,
                  int dtype, int64_t M, int64_t N, int64_t K, void* C, int c_dtype, int64_t ldc,
                  void* workspace, size_t workspace_size, void* stream);
+
+/* ----------------------------------------------------- vocabulary shards */
+/* Sum over the ranks of a vocabulary-sharded group (one process per GPU of one
+ * node) of every rank's partial d_hidden, over NVLink peer memory; no
+ * counterpart in the reference, which is single-GPU (north_star: "the partial
+ * dH is all-reduced ... over NVLink"). Only positions before each batch row's
+ * extent can carry gradient; the forward's workspace lays them out as T packed
+ * rows (the same on every rank), and the sum reads T on the device, so only
+ * those rows cross NVLink (a library collective would need T on the host).
+ * Rank q reduces packed rows [T q / N, T (q+1) / N) of every rank's partial in
+ * fp32, in rank order (deterministic), rounds once to `out_dtype` into its
+ * reduced buffer; every rank then copies each row from its owner into its own
+ * d_hidden [B,S,D] (`out_dtype`), zeros past the packed rows.
+ *   parts[r]  rank r's partial d_hidden, [B*S][D] fp32 (sparton_bwd with
+ *             d_hidden_dtype F32), complete in stream order before this call;
+ *   reds[r]   rank r's reduced-row buffer, [B*S][D] of out_dtype;
+ *   flags[r]  rank r's flag words, 2 x 8 uint32, zero before the first call;
+ *   host arrays of `world` (<= 8) device pointers, mapped into this process
+ *   (sparton_ipc_open) for r != rank;
+ *   epoch     1, 2, 3, ... : one more on every call with these buffers;
+ *   fwd_workspace  the workspace of the forward whose d_hidden this is.
+ * Every rank makes the same sequence of calls. Waits on peers are bounded
+ * (10 s); a wait that gives up records SPARTON_DEV_TIMEOUT_PEER in *status
+ * (device memory) and the result is not valid. */
+int sparton_hidden_allreduce(void* const* parts, void* const* reds, uint32_t* const* flags,
+                             int rank, int world, uint32_t epoch, const void* fwd_workspace,
+                             int64_t B, int64_t S, int64_t D, void* d_hidden, int out_dtype,
+                             uint32_t* status, void* stream);
+
+/* CUDA IPC for those buffers: export a device pointer of this process as a
+ * 64-byte handle plus its offset inside its allocation; open it in another
+ * process of the node (current device; peer access is enabled as needed);
+ * close it (the pointer sparton_ipc_open returned and the same offset). */
+int sparton_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int sparton_ipc_open(const void* handle, uint64_t offset, void** ptr);
+int sparton_ipc_close(void* ptr, uint64_t offset);
 
 /* --------------------------------------------------------------- status */
 

@@ -57,6 +57,10 @@ EXPORTED_SYMBOLS = (
     "sparton_selftest_wait_timeout",
     "sparton_gemm_workspace_size",
     "sparton_gemm",
+    "sparton_hidden_allreduce",
+    "sparton_ipc_export",
+    "sparton_ipc_open",
+    "sparton_ipc_close",
 )
 
 _lock = threading.Lock()
@@ -119,6 +123,15 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_gemm.argtypes = [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _i64, _vp, _i, _i64, _vp,
                                  _sz, _vp]
     lib.sparton_gemm.restype = _i
+    lib.sparton_hidden_allreduce.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_uint32, _vp, _i64,
+                                             _i64, _i64, _vp, _i, _vp, _vp]
+    lib.sparton_hidden_allreduce.restype = _i
+    lib.sparton_ipc_export.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]
+    lib.sparton_ipc_export.restype = _i
+    lib.sparton_ipc_open.argtypes = [_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+    lib.sparton_ipc_open.restype = _i
+    lib.sparton_ipc_close.argtypes = [_vp, ctypes.c_uint64]
+    lib.sparton_ipc_close.restype = _i
 
 
 def load() -> ctypes.CDLL:

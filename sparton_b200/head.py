@@ -38,6 +38,15 @@ REDUCE_CHUNK_BYTES = 128 << 20
 # all-reduce). Off by default: on 2 B200s with NCCL 2.28 it measured slower
 # than NCCL's all-reduce (2.8 vs 2.2 ms for 1 GiB in 8 chunks).
 REDUCE_SCATTER_GATHER = False
+# How the sharded backward sums the partial d_hidden over the group:
+#   "peer": sparton_hidden_allreduce over NVLink peer memory (sparton_b200.peer):
+#           only the packed rows (positions before each row's extent, counted on
+#           the device) cross NVLink; used when every rank of the group drives a
+#           GPU of this node, there are at most 8 of them and the reduction is in
+#           fp32; the d_weight / d_bias kernels run on a side stream meanwhile;
+#   "nccl": all-reduce of all B*S rows with NCCL, in chunks of batch rows
+#           (_HiddenGradReducer), for any group.
+HIDDEN_REDUCE = "peer"
 
 
 def row_chunks(B: int, row_bytes: int, chunk_bytes: Optional[int] = None) -> list:
@@ -148,13 +157,64 @@ class _HiddenGradReducer:
         return self.result
 
 
+def _use_peer_reduce(group, hidden, reduce_dtype) -> bool:
+    if HIDDEN_REDUCE != "peer" or reduce_dtype != torch.float32:
+        return False
+    from .peer import PeerHiddenReduce
+
+    return PeerHiddenReduce.usable(group, hidden)
+
+
+def peer_sharded_backward(grad_reps, reps, idx, hidden, weight, has_bias: bool, need_w: bool,
+                          need_b: bool, group, fwd_workspace):
+    """Backward of one rank of a vocabulary-sharded head with the d_hidden sum
+    over NVLink peer memory: the partial d_hidden into this rank's peer
+    buffer, then sparton_hidden_allreduce while the d_weight / d_bias kernels
+    run on a side stream. Returns (d_hidden, d_weight or None, d_bias or
+    None); every rank takes part, needed or not."""
+    from .peer import PeerHiddenReduce
+
+    B, S, D = hidden.shape
+    dev = hidden.device
+    grad_c = grad_reps.to(hidden.dtype).contiguous()
+    reps_c, idx_c = reps.contiguous(), idx.contiguous()
+    hidden_c, weight_c = hidden.contiguous(), weight.contiguous()
+    peer = PeerHiddenReduce.get(group, dev, B * S, D, hidden.dtype)
+    cur = torch.cuda.current_stream(dev)
+    # The partial d_hidden first, alone (every rank's reduction waits for all
+    # of them); then d_weight / d_bias on a side stream while it is summed.
+    ops.hidden_grad_rows(grad_c, reps_c, idx_c, hidden_c, weight_c, peer.partial(B, S), 0, B)
+    d_weight = d_bias = None
+    side = None
+    if need_w or need_b:
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            _, d_weight, d_bias = ops.backward_impl(grad_c, reps_c, idx_c, hidden_c, weight_c,
+                                                    need_b, need_hidden=False,
+                                                    need_embed=need_w)
+    d_hidden = torch.empty((B, S, D), dtype=hidden.dtype, device=dev)
+    peer.reduce(fwd_workspace, B, S, d_hidden)
+    if side is not None:
+        cur.wait_stream(side)
+        for t in (d_weight, d_bias):
+            if t is not None:
+                t.record_stream(cur)
+    return d_hidden, d_weight, d_bias
+
+
 class _ShardedHead(torch.autograd.Function):
     """Vocab-sharded head: local fused forward; backward = local gradients plus an
-    all-reduce (sum) of the partial d_hidden over the group."""
+    all-reduce (sum) of the partial d_hidden over the group (HIDDEN_REDUCE)."""
 
     @staticmethod
     def forward(ctx, hidden, weight, bias, mask, group, reduce_dtype):
-        reps, idx = ops.forward_impl(hidden, weight, bias, mask)
+        ctx.peer = _use_peer_reduce(group, hidden, reduce_dtype)
+        if ctx.peer:
+            reps, idx, ctx.fwd_ws = ops.forward_impl(hidden, weight, bias, mask,
+                                                     keep_workspace=True)
+        else:
+            reps, idx = ops.forward_impl(hidden, weight, bias, mask)
         ctx.save_for_backward(reps, idx, hidden, weight)
         ctx.has_bias = bias is not None
         ctx.group = group
@@ -166,6 +226,12 @@ class _ShardedHead(torch.autograd.Function):
         reps, idx, hidden, weight = ctx.saved_tensors
         need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         need_b = ctx.has_bias and ctx.needs_input_grad[2]
+        if ctx.peer:
+            d_hidden, d_weight, d_bias = peer_sharded_backward(
+                grad_reps, reps, idx, hidden, weight, ctx.has_bias, need_w, need_b, ctx.group,
+                ctx.fwd_ws)
+            return (d_hidden if need_h else None, d_weight if need_w else None,
+                    d_bias if need_b else None, None, None, None)
         # The partial d_hidden first, in chunks of batch rows, each chunk's
         # collectives overlapping the kernels of the next chunk and the last
         # ones the d_weight / d_bias kernels. Every rank takes part in the

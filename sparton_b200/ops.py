@@ -66,11 +66,12 @@ def _check_fwd_args(hidden, embed, bias, mask) -> None:
 
 
 def forward_impl(hidden: torch.Tensor, embed: torch.Tensor, bias: Optional[torch.Tensor],
-                 mask: torch.Tensor, with_idx: bool = True
-                 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+                 mask: torch.Tensor, with_idx: bool = True, keep_workspace: bool = False):
     """(reps, idx); with ``with_idx=False`` the inference forward: the kernel
     keeps the max alone, stores reps only and idx is None (no [B, V] int32 is
-    allocated or written)."""
+    allocated or written). ``keep_workspace``: also return the forward's
+    workspace (its packed-position layout, which the vocabulary-sharded
+    backward reads), as a third element."""
     _check_fwd_args(hidden, embed, bias, mask)
     lib = _lib.load()
     B, S, D = hidden.shape
@@ -89,7 +90,7 @@ def forward_impl(hidden: torch.Tensor, embed: torch.Tensor, bias: Optional[torch
                              _lib.ptr(reps), _lib.ptr(idx), _lib.ptr(ws), ws.numel(),
                              _lib.stream_handle(dev))
     _lib.check(st, "sparton_fwd")
-    return reps, idx
+    return (reps, idx, ws) if keep_workspace else (reps, idx)
 
 
 def backward_impl(grad_out: torch.Tensor, scores: torch.Tensor, idx: torch.Tensor,

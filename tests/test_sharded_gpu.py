@@ -6,7 +6,9 @@ within one bf16 rounding (rtol 1e-2) plus 1e-2 of its largest entry. Run with
 the all-reduce in one chunk, with one batch row per chunk, and with the head
 tied to a full nn.Linear decoder (tie_weights: shard-sized gradients that land
 in the decoder's rows). V = 3001 leaves a ragged last shard at every world
-size. Skipped with fewer GPUs than ranks."""
+size. Both ways of summing the partial d_hidden run: over NVLink peer memory
+(packed rows only, sparton_hidden_allreduce) and NCCL's all-reduce (in one
+chunk and one batch row per chunk). Skipped with fewer GPUs than ranks."""
 import os
 import socket
 
@@ -28,7 +30,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, reduce):
     import datetime
 
     from sparton_b200 import head as head_mod
@@ -42,6 +44,7 @@ def _worker(rank, world, port, out_dir):
     try:
         H, W, b, mask, g = synthetic(B, S, D, V, (20, S), dtype=torch.bfloat16, seed=5,
                                      w_std=0.06)
+        head_mod.HIDDEN_REDUCE = reduce
         for tag, chunk in (("one", 128 << 20), ("rows", 1), ("tied", 128 << 20)):
             head_mod.REDUCE_CHUNK_BYTES = chunk
             head = SpartonHead(V, D, use_bias=True, process_group=dist.group.WORLD).to(
@@ -70,13 +73,14 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("reduce", ["peer", "nccl"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_sharded_head_matches_single_gpu(tmp_path, world):
+def test_sharded_head_matches_single_gpu(tmp_path, world, reduce):
     from sparton_b200.head import SpartonHead
 
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), reduce), nprocs=world,
                        join=True, start_method="spawn")
     H, W, b, mask, g = synthetic(B, S, D, V, (20, S), dtype=torch.bfloat16, seed=5, w_std=0.06)
     dev = torch.device("cuda", 0)
