@@ -294,18 +294,28 @@ int sparton_transform_bwd(const void* dh, const void* y, const void* gamma, cons
  *                        contiguous; dx = dy @ W has B = W stored [K][N],
  *                        dW = dy.T @ x has A = dy, B = x stored [K][*]).
  * A, B and bias [N] are `dtype` (bf16 or f16); C [M][ldc] is `c_dtype` (dtype
- * or F32). The contiguous dimension of each operand must be a multiple of 8
- * (16-byte rows for the TMA loads); 0 < K. Long contractions over few output
- * tiles are split over the K range and the splits added in a fixed order
- * (deterministic); the workspace (256-byte aligned) holds those partials. */
+ * or F32). lda / ldb: elements per stored row of A / B (0 = dense: K for ROWS,
+ * M / N for COLS); they must be multiples of 8 (16-byte rows for the TMA
+ * loads), so a caller pads an odd extent (the vocabulary, 30522) and passes the
+ * padded row length; padding in the contraction dimension must be zero. 0 < K.
+ * Long contractions over few output tiles are split over the K range and the
+ * splits added in a fixed order (deterministic); the workspace (256-byte
+ * aligned) holds those partials. */
 #define SPARTON_LAYOUT_ROWS 0
 #define SPARTON_LAYOUT_COLS 1
 
 size_t sparton_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 
-int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const void* bias,
-                 int dtype, int64_t M, int64_t N, int64_t K, void* C, int c_dtype, int64_t ldc,
-                 void* workspace, size_t workspace_size, void* stream);
+/* Copies src [rows][cols] into dst [rows][ld] with zeros in columns cols..ld-1
+ * (bf16 / f16; ld a multiple of 8, dst 16-byte aligned): the padded operand
+ * sparton_gemm needs when a contiguous extent is not a multiple of 8 (reps
+ * [B, 30522] for the InfoNCE scores). */
+int sparton_pad_rows(const void* src, int dtype, int64_t rows, int64_t cols, void* dst,
+                     int64_t ld, void* stream);
+
+int sparton_gemm(const void* A, int a_layout, int64_t lda, const void* B, int b_layout,
+                 int64_t ldb, const void* bias, int dtype, int64_t M, int64_t N, int64_t K, void* C,
+                 int c_dtype, int64_t ldc, void* workspace, size_t workspace_size, void* stream);
 
 /* ----------------------------------------------------- vocabulary shards */
 /* Sum over the ranks of a vocabulary-sharded group (one process per GPU of one

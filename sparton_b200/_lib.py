@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "sparton_selftest_wait_timeout",
     "sparton_gemm_workspace_size",
     "sparton_gemm",
+    "sparton_pad_rows",
     "sparton_hidden_allreduce",
     "sparton_ipc_export",
     "sparton_ipc_open",
@@ -120,9 +121,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.sparton_selftest_wait_timeout.restype = _i
     lib.sparton_gemm_workspace_size.argtypes = [_i64, _i64, _i64]
     lib.sparton_gemm_workspace_size.restype = _sz
-    lib.sparton_gemm.argtypes = [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _i64, _vp, _i, _i64, _vp,
-                                 _sz, _vp]
+    lib.sparton_gemm.argtypes = [_vp, _i, _i64, _vp, _i, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i,
+                                 _i64, _vp, _sz, _vp]
     lib.sparton_gemm.restype = _i
+    lib.sparton_pad_rows.argtypes = [_vp, _i, _i64, _i64, _vp, _i64, _vp]
+    lib.sparton_pad_rows.restype = _i
     lib.sparton_hidden_allreduce.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_uint32, _vp, _i64,
                                              _i64, _i64, _vp, _i, _vp, _vp]
     lib.sparton_hidden_allreduce.restype = _i

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(256)
   extern __shared__ int hist[];  // [S]
   const int c = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   if (c == 0 && b == 0 && threadIdx.x == 0) {
     *status = 0u;
     *row_counter = 0u;
@@ -252,6 +253,8 @@ __device__ __forceinline__ int block_exclusive_scan(int x, int* tmp /*[33]*/, in
 __global__ void __launch_bounds__(1024)
     sort_scan_kernel(int S, int n_chunks, int* __restrict__ cnt, int* __restrict__ offs) {
   __shared__ int tmp[33];
+  pdl_wait();  // the chunk counts
+  pdl_trigger();
   const int b = blockIdx.x;
   int* crow = cnt + static_cast<size_t>(b) * n_chunks * S;
   int* orow = offs + static_cast<size_t>(b) * (S + 1);
@@ -289,6 +292,7 @@ __global__ void __launch_bounds__(256)
                         int2* __restrict__ ent) {
   extern __shared__ int sbase[];  // [S] bucket base of this chunk, then [nw][S] 16-bit counters
   const int c = blockIdx.x, b = blockIdx.y;
+  pdl_trigger();
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint16_t* wcnt = reinterpret_cast<uint16_t*>(sbase + S);
@@ -306,7 +310,8 @@ __global__ void __launch_bounds__(256)
   }
   const int* obase = offs + static_cast<size_t>(b) * (S + 1);
   const int* cbase = cnt + (static_cast<size_t>(b) * n_chunks + c) * S;
-  for (int i = threadIdx.x; i < S; i += blockDim.x) sbase[i] = __ldg(obase + i) + __ldg(cbase + i);
+  pdl_wait();  // the scan's offsets (the loads above read only the backward's inputs)
+  for (int i = threadIdx.x; i < S; i += blockDim.x) sbase[i] = obase[i] + cbase[i];
   for (int i = threadIdx.x; i < nw * S; i += blockDim.x) wcnt[i] = 0;
   __syncthreads();
   uint16_t* my = wcnt + warp * S;
@@ -359,6 +364,7 @@ __global__ void __launch_bounds__(256)
   __shared__ int rs[32][33];
   const int v0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  pdl_trigger();
   if (status != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *status = 0u;
   for (int i = ty; i < 32; i += 8) {
     const int b = b0 + i, v = v0 + tx;
@@ -587,6 +593,7 @@ __global__ void __launch_bounds__(kGWarps * 32, 4)
                   int slice_w, int n_slices, O* __restrict__ out, O* __restrict__ out_sum,
                   unsigned int* row_counter) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();  // the sort's CSR (dH) or the vocab-major list (dW)
   if (kMode == 0) {
     // dH: persistent warps claim items q = 0, 1, ... from the workspace counter
     // (the next claim is issued before the current one is gathered). Items are
@@ -676,14 +683,13 @@ int launch_sort(const void* grad_reps, const void* reps, const int32_t* idx, int
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sort_count_kernel launch");
   const unsigned scan_threads = static_cast<unsigned>(S >= 1024 ? 1024 : (S + 31) / 32 * 32);
-  sort_scan_kernel<<<static_cast<unsigned>(B), scan_threads, 0, stream>>>(S, n_chunks,
-                                                                          ws.sort_cnt, ws.offs);
-  e = cudaGetLastError();
+  e = launch_pdl(sort_scan_kernel, dim3(static_cast<unsigned>(B)), dim3(scan_threads), 0, stream,
+                 S, n_chunks, ws.sort_cnt, ws.offs);
   if (e != cudaSuccess) return cuda_fail(e, "sort_scan_kernel launch");
-  sort_scatter_kernel<T><<<grid, static_cast<unsigned>(nw * 32), smem_scatter, stream>>>(
-      static_cast<const T*>(grad_reps), static_cast<const T*>(reps), idx, S, V, chunk, n_chunks,
-      ws.sort_cnt, ws.offs, ws.ent);
-  e = cudaGetLastError();
+  e = launch_pdl(sort_scatter_kernel<T>, grid, dim3(static_cast<unsigned>(nw * 32)), smem_scatter,
+                 stream, static_cast<const T*>(grad_reps), static_cast<const T*>(reps), idx, S, V,
+                 chunk, n_chunks, static_cast<const int*>(ws.sort_cnt),
+                 static_cast<const int*>(ws.offs), ws.ent);
   if (e != cudaSuccess) return cuda_fail(e, "sort_scatter_kernel launch");
   return SPARTON_OK;
 }
@@ -721,10 +727,8 @@ int launch_gather_nc(const T* src, int B, int S, int D, int V, const int* offs, 
   const long long need = (static_cast<long long>(n_rows) + kGWarps - 1) / kGWarps * n_slices;
   const long long cap = kMode == 0 ? static_cast<long long>(bps) * device_sm_count() : need;
   const unsigned grid = static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
-  gather_kernel<T, O, NC, G, U, kMode><<<grid, block, 0, stream>>>(
-      src, B, S, D, V, offs, ent, n_rows, slice_w, n_slices, out, out_sum,
-      row_counter);
-  e = cudaGetLastError();
+  e = launch_pdl(gather_kernel<T, O, NC, G, U, kMode>, dim3(grid), dim3(block), 0, stream, src, B,
+                 S, D, V, offs, ent, n_rows, slice_w, n_slices, out, out_sum, row_counter);
   if (e != cudaSuccess) return cuda_fail(e, "gather_kernel launch");
   return SPARTON_OK;
 }

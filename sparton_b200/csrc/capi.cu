@@ -232,9 +232,9 @@ size_t sparton_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return gemm_workspace_bytes(M, N, K);
 }
 
-int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const void* bias,
-                 int dtype, int64_t M, int64_t N, int64_t K, void* C, int c_dtype, int64_t ldc,
-                 void* workspace, size_t workspace_size, void* stream) {
+int sparton_gemm(const void* A, int a_layout, int64_t lda, const void* B, int b_layout,
+                 int64_t ldb, const void* bias, int dtype, int64_t M, int64_t N, int64_t K, void* C,
+                 int c_dtype, int64_t ldc, void* workspace, size_t workspace_size, void* stream) {
   if (dtype != SPARTON_DTYPE_BF16 && dtype != SPARTON_DTYPE_F16)
     return fail(SPARTON_ERR_UNSUPPORTED, "sparton_gemm takes bf16 or f16 operands (dtype %d)",
                 dtype);
@@ -248,14 +248,19 @@ int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const
                 (long long)M, (long long)N, (long long)K);
   if (ldc < N) return fail(SPARTON_ERR_INVALID_ARGUMENT, "ldc=%lld < N=%lld", (long long)ldc,
                            (long long)N);
-  // TMA: every row of an operand starts on a 16-byte boundary.
+  // TMA: every stored row of an operand starts on a 16-byte boundary.
   const int64_t a_inner = a_layout == SPARTON_LAYOUT_ROWS ? K : M;
   const int64_t b_inner = b_layout == SPARTON_LAYOUT_ROWS ? K : N;
-  if (a_inner % 8 != 0 || b_inner % 8 != 0)
+  if (lda == 0) lda = a_inner;
+  if (ldb == 0) ldb = b_inner;
+  if (lda < a_inner || ldb < b_inner)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "lda=%lld / ldb=%lld below the rows' extent",
+                (long long)lda, (long long)ldb);
+  if (lda % 8 != 0 || ldb % 8 != 0 || lda > (1ll << 31) || ldb > (1ll << 31))
     return fail(SPARTON_ERR_UNSUPPORTED,
-                "the contiguous dimension of each operand must be a multiple of 8 (A: %lld, B: "
-                "%lld)",
-                (long long)a_inner, (long long)b_inner);
+                "stored operand rows must hold a multiple of 8 elements (A: %lld, B: %lld); pad "
+                "the contiguous dimension",
+                (long long)lda, (long long)ldb);
   SPARTON_TRY(check_workspace(workspace, workspace_size, gemm_workspace_bytes(M, N, K)));
   if (M == 0 || N == 0) return SPARTON_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
@@ -270,8 +275,25 @@ int sparton_gemm(const void* A, int a_layout, const void* B, int b_layout, const
     return fail(SPARTON_ERR_UNSUPPORTED, "K == 0 is not supported");
   }
   return launch_gemm(dtype, c_dtype, a_layout == SPARTON_LAYOUT_COLS,
-                     b_layout == SPARTON_LAYOUT_COLS, A, B, bias, static_cast<int>(M),
+                     b_layout == SPARTON_LAYOUT_COLS, A, lda, B, ldb, bias, static_cast<int>(M),
                      static_cast<int>(N), static_cast<int>(K), C, ldc, workspace, st);
+}
+
+int sparton_pad_rows(const void* src, int dtype, int64_t rows, int64_t cols, void* dst,
+                     int64_t ld, void* stream) {
+  if (dtype != SPARTON_DTYPE_BF16 && dtype != SPARTON_DTYPE_F16)
+    return fail(SPARTON_ERR_UNSUPPORTED, "sparton_pad_rows takes bf16 or f16 (dtype %d)", dtype);
+  if (rows < 0 || cols < 0 || ld < cols || rows > (1ll << 31) - 1 || ld > (1ll << 31) - 1)
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "bad sizes (rows=%lld cols=%lld ld=%lld)",
+                (long long)rows, (long long)cols, (long long)ld);
+  if (ld % 8 != 0 || !aligned(dst, 16))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "dst rows must be 16-byte aligned (ld %% 8 == 0)");
+  if (rows == 0 || ld == 0) return SPARTON_OK;
+  if (dst == nullptr || (cols > 0 && src == nullptr))
+    return fail(SPARTON_ERR_INVALID_ARGUMENT, "src / dst is NULL");
+  SPARTON_TRY(check_device());
+  return launch_pad_rows(dtype, src, static_cast<int>(rows), static_cast<int>(cols), dst,
+                         static_cast<int>(ld), static_cast<cudaStream_t>(stream));
 }
 
 int sparton_read_device_status(const void* workspace, void* stream, uint32_t* code) {

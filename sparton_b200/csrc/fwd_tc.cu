@@ -603,6 +603,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_addr(tmem_holder), kTmemCols);
     tmem_relinquish();
   }
+  // Everything above overlaps the end of pack_prepare_kernel (programmatic
+  // dependent launch); its results are read from here on.
+  pdl_wait();
   const Partition q = choose_partition(p, reinterpret_cast<float*>(smem + kPartOffset),
                                        reinterpret_cast<int*>(smem + kPartOffset) + kThreads / 32);
   tc_fence_before_sync();
@@ -652,8 +655,8 @@ int launch_kernel(const CUtensorMap& tmW, const HiddenMaps& tmH, const FwdTcPara
       attr_done[dev] = true;
     }
   }
-  fwd_tc_kernel<T, kFmt, kIdx><<<grid, kThreads, kSmemBytes, stream>>>(tmW, tmH, p);
-  e = cudaGetLastError();
+  e = launch_pdl(fwd_tc_kernel<T, kFmt, kIdx>, dim3(grid), dim3(kThreads), kSmemBytes, stream, tmW,
+                 tmH, p);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_tc_kernel launch");
   return SPARTON_OK;
 }

@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <mutex>
+#include <string.h>
 
 #include "dtype.cuh"
 #include "internal.h"
@@ -67,17 +68,24 @@ constexpr int kCtrlOffset = kStages * kStageBytes;
 constexpr int kTmemHolderOffset = kCtrlOffset + kNumBars * 8;
 constexpr int kAbortOffset = kTmemHolderOffset + 4;
 constexpr int kCtrlBytes = 256;
-constexpr int kSmemBytes = kCtrlOffset + kCtrlBytes + 1024;
+// Epilogue staging for outputs whose rows are not 16-byte aligned: one 32 x 33
+// fp32 tile per epilogue warp, so a row is stored by consecutive lanes.
+constexpr int kStageTileOffset = kCtrlOffset + kCtrlBytes;
+constexpr int kStageTileBytes = kEpiWarps * 32 * 33 * 4;
+constexpr int kSmemBytes = kStageTileOffset + kStageTileBytes + 1024;
 
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, splits, kb_per_split;
+  int bn;             // output columns per tile: 256, 192 or 128 (a multiple of 64)
   long long units;
   const void* bias;   // [N] in the output's element type family (T), or NULL
   void* C;            // [M][ldc] of type O (splits == 1)
   long long ldc;
   float* partial;     // [splits][M][N] fp32 (splits > 1)
   bool vec_store;     // rows of C start on 16-byte boundaries
+  bool vec_bias;      // bias starts on a 16-byte boundary
+  bool vec_partial;   // N % 4 == 0: partial rows take 16-byte stores
   unsigned int* status;
 };
 
@@ -97,7 +105,7 @@ __device__ __forceinline__ UnitPos unit_pos(const GemmParams& p, long long u) {
   o.split = static_cast<int>(u / tiles);
   const int t = static_cast<int>(u - static_cast<long long>(o.split) * tiles);
   o.m0 = (t / p.n_tiles) * kBM;
-  o.n0 = (t % p.n_tiles) * kBN;
+  o.n0 = (t % p.n_tiles) * p.bn;
   o.kb0 = o.split * p.kb_per_split;
   o.kb1 = min(p.k_blocks, o.kb0 + p.kb_per_split);
   return o;
@@ -107,7 +115,7 @@ __device__ __forceinline__ UnitPos unit_pos(const GemmParams& p, long long u) {
 template <bool kAmn, bool kBmn>
 __device__ __forceinline__ void load_stage(const CUtensorMap* tmA, const CUtensorMap* tmB,
                                            uint32_t a_dst, uint32_t full, const UnitPos& u,
-                                           int kb) {
+                                           int kb, int bn) {
   const int k0 = kb * kBK;
   if (kAmn) {
 #pragma unroll
@@ -118,7 +126,8 @@ __device__ __forceinline__ void load_stage(const CUtensorMap* tmA, const CUtenso
   const uint32_t b_dst = a_dst + kABytes;
   if (kBmn) {
 #pragma unroll
-    for (int i = 0; i < kBN / 64; ++i) tma_load_2d(b_dst + i * kBoxBytes, tmB, full, u.n0 + 64 * i, k0);
+    for (int i = 0; i < kBN / 64; ++i)
+      if (64 * i < bn) tma_load_2d(b_dst + i * kBoxBytes, tmB, full, u.n0 + 64 * i, k0);
   } else {
     tma_load_2d(b_dst, tmB, full, k0, u.n0);
   }
@@ -141,8 +150,9 @@ __device__ void run_producer(const GemmParams& p, const CUtensorMap* tmA, const 
       }
       if (elect_one()) {
         const uint32_t full = c.bar(kBarFull + stage);
-        mbar_arrive_expect_tx(full, kStageBytes);  // out-of-range parts are zero-filled
-        load_stage<kAmn, kBmn>(tmA, tmB, stage_base + stage * kStageBytes, full, up, kb);
+        // out-of-range parts of a box are zero-filled and counted
+        mbar_arrive_expect_tx(full, static_cast<uint32_t>(kABytes + p.bn * kBK * 2));
+        load_stage<kAmn, kBmn>(tmA, tmB, stage_base + stage * kStageBytes, full, up, kb, p.bn);
       }
       __syncwarp();
       issued_mask |= 1u << stage;
@@ -190,7 +200,7 @@ __device__ void run_mma(const GemmParams& p, uint32_t stage_base, uint32_t tmem_
       break;
     }
     tc_fence_after_sync();
-    const uint32_t n_mma = static_cast<uint32_t>(min(kBN, (p.N - up.n0 + 15) / 16 * 16));
+    const uint32_t n_mma = static_cast<uint32_t>(min(p.bn, (p.N - up.n0 + 15) / 16 * 16));
     const uint32_t idesc = umma_idesc_f16(kFmt, kBM, n_mma) | (kAmn ? (1u << 15) : 0u) |
                            (kBmn ? (1u << 16) : 0u);
     const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
@@ -257,9 +267,25 @@ __device__ __forceinline__ void store_row_chunk(const GemmParams& p, int m, int 
   }
 }
 
+// Stores the warp's 32 rows x 32 columns (lane l holds row m0 + l) through a
+// shared tile, one row per step by consecutive lanes: coalesced stores for
+// outputs whose rows are not 16-byte aligned (C with an odd row length).
+template <typename O>
+__device__ __forceinline__ void store_chunk_staged(const GemmParams& p, float* tile, int m0, int n,
+                                                   const float (&v)[32], int lane) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = v[i];
+  __syncwarp();
+  const int cnt = min(32, p.N - n);
+  O* base = static_cast<O*>(p.C) + n + lane;
+  for (int r = 0; r < 32 && m0 + r < p.M; ++r)
+    if (lane < cnt) base[static_cast<size_t>(m0 + r) * p.ldc] = from_f32<O>(tile[r * 33 + lane]);
+  __syncwarp();
+}
+
 template <typename T, typename O>
 __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
-                             int lane) {
+                             int lane, float* stage_tile) {
   const int quad = warp & 3;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
   uint32_t tile = 0;
@@ -272,31 +298,58 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
     if (!__all_sync(0xFFFFFFFFu, got)) break;
     tc_fence_after_sync();
     const int m = up.m0 + quad * 32 + lane;
-    const int nch = (min(kBN, p.N - up.n0) + 31) >> 5;
+    const int nch = (min(p.bn, p.N - up.n0) + 31) >> 5;
     for (int ch = 0; ch < nch; ++ch) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(lane_base + static_cast<uint32_t>(acc * kBN + 32 * ch), r);
       tmem_ld_wait(r);
       const int n = up.n0 + 32 * ch;
-      if (m >= p.M) continue;
+      const bool row_ok = m < p.M;
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const int cnt = min(32, p.N - n);
       if (p.splits > 1) {
-        float* dst = p.partial + (static_cast<size_t>(up.split) * p.M + m) * p.N + n;
-        const int cnt = min(32, p.N - n);
+        // (no early exit: the TMEM load of the next chunk is warp-collective)
+        float* dst = p.partial + (static_cast<size_t>(up.split) * p.M + (row_ok ? m : 0)) * p.N + n;
+        if (!row_ok) {
+        } else if (p.vec_partial && cnt == 32) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < cnt) dst[i] = v[i];
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < cnt) dst[i] = v[i];
+        }
       } else {
         if (p.bias != nullptr) {
           const T* bp = static_cast<const T*>(p.bias) + n;
-          const int cnt = min(32, p.N - n);
+          if (p.vec_bias && cnt == 32) {
+            // 32 bias values in four 16-byte loads (the same for every lane)
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < cnt) v[i] += to_f32<T>(bp[i]);
+            for (int j = 0; j < 4; ++j) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(bp) + j);
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                T pair[2];
+                memcpy(pair, &ws[h], 4);
+                v[8 * j + 2 * h] += to_f32<T>(pair[0]);
+                v[8 * j + 2 * h + 1] += to_f32<T>(pair[1]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < cnt) v[i] += to_f32<T>(bp[i]);
+          }
         }
-        store_row_chunk<O>(p, m, n, v);
+        if (p.vec_store) {
+          if (row_ok) store_row_chunk<O>(p, m, n, v);
+        } else {
+          store_chunk_staged<O>(p, stage_tile, up.m0 + quad * 32, n, v, lane);
+        }
       }
     }
     tc_fence_before_sync();
@@ -352,7 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     run_mma<kFmt, kAmn, kBmn>(p, stage_base, tmem_base, c);
     __syncwarp();
   } else {
-    run_epilogue<T, O>(p, tmem_base, c, warp, lane);
+    run_epilogue<T, O>(p, tmem_base, c, warp, lane,
+                       reinterpret_cast<float*>(smem + kStageTileOffset) + (warp - 2) * 32 * 33);
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -362,16 +416,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// C[m, n] = sum over splits (in order) of partial[s][m][n] (+ bias[n]).
+// C[m, n] = sum over splits (in order) of partial[s][m][n] (+ bias[n]); the
+// loads of eight splits are issued before they are added.
 template <typename T, typename O>
 __global__ void __launch_bounds__(256) gemm_reduce_kernel(const float* __restrict__ partial,
                                                           int splits, int M, int N,
                                                           const T* __restrict__ bias, O* C,
                                                           long long ldc) {
+  pdl_wait();  // the split partials
   const long long total = static_cast<long long>(M) * N;
   for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += 256ll * gridDim.x) {
     float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += __ldcs(partial + k * total + i);
+    for (int k0 = 0; k0 < splits; k0 += 8) {
+      float x[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = k0 + j < splits ? __ldcs(partial + (k0 + j) * total + i) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += x[j];
+    }
     const int m = static_cast<int>(i / N), n = static_cast<int>(i - static_cast<long long>(m) * N);
     if (bias != nullptr) s += to_f32<T>(bias[n]);
     C[static_cast<size_t>(m) * ldc + n] = from_f32<O>(s);
@@ -379,19 +441,35 @@ __global__ void __launch_bounds__(256) gemm_reduce_kernel(const float* __restric
 }
 
 // ----------------------------------------------------------------------- host
-// Splits of the K range: enough units for about two per SM when the output has
-// few tiles, each split at least 4 k blocks; a function of the shape only.
-constexpr long long kTargetUnits = 296;
+// Splits of the K range when the output has few tiles: about one unit per SM
+// of a B200 (148; a constant, so the split count and the workspace size depend
+// on the shape only), each split at least 4 k blocks.
+constexpr long long kTargetUnits = 148;
 
+// Output tile width bn: 256 unless the tiles fill the GPU in several rounds,
+// then the width (256, 192 or 128) with the fewest rounds x (bn + 64) (64
+// columns' worth of per-tile cost), so that the last round is not mostly idle.
 void plan(int M, int N, int K, int& m_tiles, int& n_tiles, int& k_blocks, int& splits,
-          int& kb_per) {
+          int& kb_per, int& bn) {
   m_tiles = (M + kBM - 1) / kBM;
-  n_tiles = (N + kBN - 1) / kBN;
   k_blocks = (K + kBK - 1) / kBK;
+  bn = kBN;
+  if (static_cast<long long>(m_tiles) * ((N + kBN - 1) / kBN) >= kTargetUnits) {
+    long long best = -1;
+    for (int w : {256, 192, 128}) {
+      const long long t = static_cast<long long>(m_tiles) * ((N + w - 1) / w);
+      const long long cost = (t + kTargetUnits - 1) / kTargetUnits * (w + 64);
+      if (best < 0 || cost < best) {
+        best = cost;
+        bn = w;
+      }
+    }
+  }
+  n_tiles = (N + bn - 1) / bn;
   const long long tiles = static_cast<long long>(m_tiles) * n_tiles;
   long long s = 1;
-  if (tiles < kTargetUnits / 2 && k_blocks >= 8) {
-    s = (kTargetUnits + tiles - 1) / tiles;
+  if (2 * tiles <= kTargetUnits && k_blocks >= 8) {
+    s = kTargetUnits / tiles;
     s = s < k_blocks / 4 ? s : k_blocks / 4;
     if (s < 1) s = 1;
   }
@@ -399,36 +477,50 @@ void plan(int M, int N, int K, int& m_tiles, int& n_tiles, int& k_blocks, int& s
   splits = (k_blocks + kb_per - 1) / kb_per;  // every split has >= 1 k block
 }
 
+struct GemmArgs {
+  const void* A;
+  const void* B;
+  long long lda, ldb;  // elements per stored row of A and B (>= their contiguous extent)
+  const void* bias;
+  int M, N, K;
+  void* C;
+  long long ldc;
+  void* workspace;
+};
+
+// K-major: rows of `ld` elements, logical [mn][K], box [box_rows x 64 k];
+// MN-major: rows of `ld` elements, logical [K][mn], box [64 k x 64 mn]. The
+// map's extent is the stored one (ld), so a padded operand reads its padding.
 int make_operand_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, bool mn_major,
-                     int mn, int K, int box_rows) {
-  // K-major: [mn][K], box [box_rows x 64 k]; MN-major: [K][mn], box [64 k x 64 mn].
+                     int mn, int K, long long ld, int box_rows) {
   if (mn_major)
-    return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(mn), static_cast<uint64_t>(K),
-                              static_cast<uint64_t>(mn) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
-  return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(K), static_cast<uint64_t>(mn),
-                            static_cast<uint64_t>(K) * 2, kBK, static_cast<uint32_t>(box_rows),
+    return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(ld), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(ld) * 2, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_tensor_map_2d(map, dt, base, static_cast<uint64_t>(ld), static_cast<uint64_t>(mn),
+                            static_cast<uint64_t>(ld) * 2, kBK, static_cast<uint32_t>(box_rows),
                             CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <typename T, typename O, uint32_t kFmt, bool kAmn, bool kBmn>
-int launch_typed(CUtensorMapDataType dt, const void* A, const void* B, const void* bias, int M,
-                 int N, int K, void* C, long long ldc, void* workspace, cudaStream_t stream) {
+int launch_typed(CUtensorMapDataType dt, const GemmArgs& a, cudaStream_t stream) {
   GemmParams p;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  plan(M, N, K, p.m_tiles, p.n_tiles, p.k_blocks, p.splits, p.kb_per_split);
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  plan(a.M, a.N, a.K, p.m_tiles, p.n_tiles, p.k_blocks, p.splits, p.kb_per_split, p.bn);
   p.units = static_cast<long long>(p.m_tiles) * p.n_tiles * p.splits;
-  p.bias = bias;
-  p.C = C;
-  p.ldc = ldc;
-  p.status = static_cast<unsigned int*>(workspace);
-  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
-  p.vec_store = (reinterpret_cast<uintptr_t>(C) % 16 == 0) && ((ldc * sizeof(O)) % 16 == 0);
+  p.bias = a.bias;
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.status = static_cast<unsigned int*>(a.workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256);
+  p.vec_store = (reinterpret_cast<uintptr_t>(a.C) % 16 == 0) && ((a.ldc * sizeof(O)) % 16 == 0);
+  p.vec_bias = reinterpret_cast<uintptr_t>(a.bias) % 16 == 0;
+  p.vec_partial = a.N % 4 == 0;
   CUtensorMap tmA, tmB;
-  int st = make_operand_map(&tmA, dt, A, kAmn, M, K, kBM);
+  int st = make_operand_map(&tmA, dt, a.A, kAmn, a.M, a.K, a.lda, kBM);
   if (st != SPARTON_OK) return st;
-  st = make_operand_map(&tmB, dt, B, kBmn, N, K, kBN);
+  st = make_operand_map(&tmB, dt, a.B, kBmn, a.N, a.K, a.ldb, p.bn);
   if (st != SPARTON_OK) return st;
 
   static std::mutex mu;
@@ -445,7 +537,7 @@ int launch_typed(CUtensorMapDataType dt, const void* A, const void* B, const voi
       attr_done[dev] = true;
     }
   }
-  e = cudaMemsetAsync(workspace, 0, 256, stream);  // status word
+  e = cudaMemsetAsync(a.workspace, 0, 256, stream);  // status word
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
   const long long sms = device_sm_count();
   const unsigned grid = static_cast<unsigned>(p.units < sms ? p.units : sms);
@@ -453,56 +545,97 @@ int launch_typed(CUtensorMapDataType dt, const void* A, const void* B, const voi
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm_tc_kernel launch");
   if (p.splits > 1) {
-    const long long total = static_cast<long long>(M) * N;
+    const long long total = static_cast<long long>(a.M) * a.N;
     long long blocks = (total + 255) / 256;
     if (blocks > 4 * sms) blocks = 4 * sms;
-    gemm_reduce_kernel<T, O><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        p.partial, p.splits, M, N, static_cast<const T*>(bias), static_cast<O*>(C), ldc);
-    e = cudaGetLastError();
+    e = launch_pdl(gemm_reduce_kernel<T, O>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                   stream, static_cast<const float*>(p.partial), p.splits, a.M, a.N,
+                   static_cast<const T*>(a.bias), static_cast<O*>(a.C), a.ldc);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_reduce_kernel launch");
   }
   return SPARTON_OK;
 }
 
 template <typename T, uint32_t kFmt, bool kAmn, bool kBmn>
-int launch_out(CUtensorMapDataType dt, int c_dtype, const void* A, const void* B,
-               const void* bias, int M, int N, int K, void* C, long long ldc, void* ws,
-               cudaStream_t s) {
-  if (c_dtype == SPARTON_DTYPE_F32)
-    return launch_typed<T, float, kFmt, kAmn, kBmn>(dt, A, B, bias, M, N, K, C, ldc, ws, s);
-  return launch_typed<T, T, kFmt, kAmn, kBmn>(dt, A, B, bias, M, N, K, C, ldc, ws, s);
+int launch_out(CUtensorMapDataType dt, int c_dtype, const GemmArgs& a, cudaStream_t s) {
+  if (c_dtype == SPARTON_DTYPE_F32) return launch_typed<T, float, kFmt, kAmn, kBmn>(dt, a, s);
+  return launch_typed<T, T, kFmt, kAmn, kBmn>(dt, a, s);
 }
 
 template <typename T, uint32_t kFmt>
-int launch_layouts(CUtensorMapDataType dt, int c_dtype, bool a_mn, bool b_mn, const void* A,
-                   const void* B, const void* bias, int M, int N, int K, void* C, long long ldc,
-                   void* ws, cudaStream_t s) {
-  if (!a_mn && !b_mn)
-    return launch_out<T, kFmt, false, false>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
-  if (!a_mn && b_mn)
-    return launch_out<T, kFmt, false, true>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
-  if (a_mn && !b_mn)
-    return launch_out<T, kFmt, true, false>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
-  return launch_out<T, kFmt, true, true>(dt, c_dtype, A, B, bias, M, N, K, C, ldc, ws, s);
+int launch_layouts(CUtensorMapDataType dt, int c_dtype, bool a_mn, bool b_mn, const GemmArgs& a,
+                   cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_out<T, kFmt, false, false>(dt, c_dtype, a, s);
+  if (!a_mn && b_mn) return launch_out<T, kFmt, false, true>(dt, c_dtype, a, s);
+  if (a_mn && !b_mn) return launch_out<T, kFmt, true, false>(dt, c_dtype, a, s);
+  return launch_out<T, kFmt, true, true>(dt, c_dtype, a, s);
+}
+
+// dst[r][c] = src[r][c] for c < cols, 0 for cols <= c < ld; dst rows (ld
+// elements) start on 16-byte boundaries, src rows (cols elements) on 2-byte
+// ones. One warp per (row, segment of 2048 columns), 8 destination elements (16
+// bytes) per lane and step.
+constexpr int kPadSeg = 2048;
+
+template <typename T>
+__global__ void __launch_bounds__(256) pad_rows_kernel(const T* __restrict__ src, int rows,
+                                                       int cols, T* __restrict__ dst, int ld) {
+  const long long warp = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+  const long long nwarps = (gridDim.x * static_cast<long long>(blockDim.x)) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int segs = (ld + kPadSeg - 1) / kPadSeg;
+  for (long long w = warp; w < static_cast<long long>(rows) * segs; w += nwarps) {
+    const int r = static_cast<int>(w / segs), seg = static_cast<int>(w - static_cast<long long>(r) * segs);
+    const T* s = src + static_cast<size_t>(r) * cols;
+    T* d = dst + static_cast<size_t>(r) * ld;
+    const int c_end = min(ld, (seg + 1) * kPadSeg);
+    for (int c0 = seg * kPadSeg + lane * 8; c0 < c_end; c0 += 256) {
+      T v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = c0 + i < cols ? s[c0 + i] : from_f32<T>(0.f);
+      uint4 w4;
+      memcpy(&w4, v, 16);
+      *reinterpret_cast<uint4*>(d + c0) = w4;
+    }
+  }
 }
 
 }  // namespace
 
+int launch_pad_rows(int dtype, const void* src, int rows, int cols, void* dst, int ld,
+                    cudaStream_t stream) {
+  const long long need =
+      (static_cast<long long>(rows) * ((ld + kPadSeg - 1) / kPadSeg) + 7) / 8;
+  const unsigned grid = static_cast<unsigned>(need < 8ll * device_sm_count() ? (need > 0 ? need : 1)
+                                                                             : 8 * device_sm_count());
+  if (dtype == SPARTON_DTYPE_BF16)
+    pad_rows_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(src), rows, cols, static_cast<__nv_bfloat16*>(dst), ld);
+  else if (dtype == SPARTON_DTYPE_F16)
+    pad_rows_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(src), rows, cols,
+                                                     static_cast<__half*>(dst), ld);
+  else
+    return fail(SPARTON_ERR_UNSUPPORTED, "sparton_pad_rows takes bf16 or f16");
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "pad_rows_kernel launch");
+}
+
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  int mt, nt, kb, splits, kbp;
-  plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), mt, nt, kb, splits, kbp);
+  int mt, nt, kb, splits, kbp, bn;
+  plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), mt, nt, kb, splits, kbp, bn);
   return 256 + (splits > 1 ? static_cast<size_t>(splits) * M * N * 4 : 0);
 }
 
-int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, const void* B,
-                const void* bias, int M, int N, int K, void* C, long long ldc, void* workspace,
-                cudaStream_t stream) {
+int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, long long lda,
+                const void* B, long long ldb, const void* bias, int M, int N, int K, void* C,
+                long long ldc, void* workspace, cudaStream_t stream) {
+  const GemmArgs a{A, B, lda, ldb, bias, M, N, K, C, ldc, workspace};
   if (dtype == SPARTON_DTYPE_BF16)
     return launch_layouts<__nv_bfloat16, 1u>(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c_dtype, a_mn, b_mn,
-                                             A, B, bias, M, N, K, C, ldc, workspace, stream);
+                                             a, stream);
   if (dtype == SPARTON_DTYPE_F16)
-    return launch_layouts<__half, 0u>(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, c_dtype, a_mn, b_mn, A, B,
-                                      bias, M, N, K, C, ldc, workspace, stream);
+    return launch_layouts<__half, 0u>(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, c_dtype, a_mn, b_mn, a,
+                                      stream);
   return fail(SPARTON_ERR_UNSUPPORTED, "the tensor-core GEMM takes bf16 or f16 operands");
 }
 

@@ -201,6 +201,43 @@ int launch_reps_csr(int dtype, const void* reps, int B, int V, float threshold, 
 int launch_reps_topk(int dtype, const void* reps, int B, int V, int k, void* vals, int32_t* idx,
                      cudaStream_t stream);
 
+// Launch of a kernel that depends on the previous work of its stream, with
+// programmatic dependent launch (PDL): the launch may begin while the
+// predecessor's last CTAs are still running, and the kernel waits for the
+// predecessor's results with pdl_wait() (griddepcontrol.wait) before it reads
+// them. For short kernels in a chain (sort, CSR, regularisers) this hides the
+// launch gap. A kernel that calls pdl_wait() is also correct when launched
+// without the attribute (the wait then returns at once).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Device side of launch_pdl: wait until the grids this one depends on have
+// completed and their memory operations are visible.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Called at the start of a kernel that has a launch_pdl successor: once every
+// CTA of this grid has called it (i.e. the last wave is running), the
+// successor may begin launching into the freed slots; it still waits in
+// pdl_wait() for this grid to complete before reading its results.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Whether clusters of P CTAs with `smem` bytes each can be resident, asked once
 // per (device, P, smem) of the occupancy API and remembered.
 template <typename K>
@@ -241,11 +278,17 @@ int launch_transform_bwd(int dtype, const void* dh, const void* y, const void* g
 // Plain tensor-core GEMM (gemm_tc.cu): C[M,N] = sum_k A[m,k] B[n,k] (+ bias[n]);
 // a_mn / b_mn: the operand is stored MN-major ([K][M] / [K][N]) instead of
 // K-major ([M][K] / [N][K]). dtype: bf16 / f16 operands (and bias); c_dtype:
-// dtype or F32. The workspace holds a 256-byte header and the split partials.
+// dtype or F32; lda / ldb: elements per stored row of A / B (>= the operand's
+// contiguous extent: K for K-major, M / N for MN-major; padding is read as part
+// of the operand and must be zero). The workspace holds a 256-byte header and
+// the split partials.
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
-int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, const void* B,
-                const void* bias, int M, int N, int K, void* C, long long ldc, void* workspace,
-                cudaStream_t stream);
+// dst [rows][ld] = src [rows][cols] with zero columns cols..ld-1 (16-bit types).
+int launch_pad_rows(int dtype, const void* src, int rows, int cols, void* dst, int ld,
+                    cudaStream_t stream);
+int launch_gemm(int dtype, int c_dtype, bool a_mn, bool b_mn, const void* A, long long lda,
+                const void* B, long long ldb, const void* bias, int M, int N, int K, void* C,
+                long long ldc, void* workspace, cudaStream_t stream);
 
 int launch_bwd(int dtype, const void* grad_reps, const void* reps, const int32_t* idx,
                const void* hidden, const void* weight, int B, int S, int D, int V,

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(256) mask_prepare_kernel(const M* __restrict__
                                                            unsigned int* header) {
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   if (b == 0 && threadIdx.x < 3) header[threadIdx.x] = 0u;
   const M* row = mask + static_cast<size_t>(b) * S;
   int last = 0;
@@ -97,6 +98,8 @@ __global__ void __launch_bounds__(kPackThreads)
                         int* prows, uint32_t* pvalid, uint32_t* prow, unsigned int* total_cols) {
   __shared__ int sh[kPackThreads / 32 + 1];
   const int tid = threadIdx.x;
+  pdl_wait();  // extents and bits of mask_prepare_kernel
+  pdl_trigger();
   // 1. packed length and start of every row; the rows with columns, in order.
   int carry = 0, carry_nz = 0;
   for (int base = 0; base < B; base += kPackThreads) {
@@ -149,10 +152,9 @@ int launch_typed(const void* mask, int B, int S, const FwdWorkspace& ws, cudaStr
                                                 ws.extent, ws.status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "mask_prepare_kernel launch");
-  pack_prepare_kernel<<<1, kPackThreads, 0, stream>>>(B, ws.S32, ws.extent, ws.bits, ws.pcol,
-                                                      ws.plen, ws.pnz, ws.prows, ws.pvalid,
-                                                      ws.prow, ws.total_cols);
-  e = cudaGetLastError();
+  e = launch_pdl(pack_prepare_kernel, dim3(1), dim3(kPackThreads), 0, stream, B, ws.S32,
+                 static_cast<const int*>(ws.extent), static_cast<const uint32_t*>(ws.bits),
+                 ws.pcol, ws.plen, ws.pnz, ws.prows, ws.pvalid, ws.prow, ws.total_cols);
   if (e != cudaSuccess) return cuda_fail(e, "pack_prepare_kernel launch");
   return SPARTON_OK;
 }

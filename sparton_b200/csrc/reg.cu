@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(kRegWarps * 32)
   __shared__ float s_col[kRegWarps][32];
   __shared__ float s_abs[kRegWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   const int v = blockIdx.x * 32 + lane;
   float col = 0.f, ab = 0.f;
   if (v < V) {
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(kTotalThreads)
     reg_total_kernel(const float* __restrict__ partials, int nblocks, float scale_l1,
                      float scale_flops, float* __restrict__ totals) {
   __shared__ float s[2][kTotalThreads / 32];
+  pdl_wait();  // the block partials
   float a = 0.f, q = 0.f;
   for (int i = threadIdx.x; i < nblocks; i += kTotalThreads) {
     a += partials[2 * i];
@@ -130,9 +132,8 @@ int launch_fwd_typed(const void* reps, int B, int V, float scale_l1, float scale
                                                             colsum, partials);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reg_fwd_kernel launch");
-  reg_total_kernel<<<1, kTotalThreads, 0, stream>>>(partials, nblocks, scale_l1, scale_flops,
-                                                     totals);
-  e = cudaGetLastError();
+  e = launch_pdl(reg_total_kernel, dim3(1), dim3(kTotalThreads), 0, stream,
+                 static_cast<const float*>(partials), nblocks, scale_l1, scale_flops, totals);
   if (e != cudaSuccess) return cuda_fail(e, "reg_total_kernel launch");
   return SPARTON_OK;
 }

@@ -17,7 +17,9 @@
 //                     caller sees nnz in crow[B]).
 // Top-k, a cluster of up to 8 CTAs per row (enough CTAs for two per SM):
 //   radix select on order-preserving unsigned keys (8 bits a pass: 2 passes
-//   for 16-bit types, 4 for fp32), the CTAs' histograms summed through
+//   for 16-bit types, 4 for fp32; shared-memory histograms in which the lanes
+//   holding the common digit, that of 0.0, add once), the CTAs' histograms
+//   summed through
 //   distributed shared memory, finds the k-th largest key K and how many of
 //   its equals to take; one ordered pass collects the entries above K and the
 //   first such equals in vocab order into CTA 0; a bitonic sort in its shared
@@ -108,6 +110,7 @@ __global__ void __launch_bounds__(kCsrThreads)
   const int b = blockIdx.y, ch = blockIdx.x;
   const int v0 = ch * kCsrChunk, v1 = min(V, v0 + kCsrChunk);
   const T* row = reps + static_cast<size_t>(b) * V;
+  pdl_trigger();
   int n = 0;
   for (int base = v0 + warp * 32 * kTileU; base < v1; base += kCsrThreads * kTileU) {
     T x[kTileU];
@@ -129,6 +132,8 @@ __global__ void __launch_bounds__(1024)
   __shared__ int tmp[32];
   const int n = B * nchunks;
   int carry = 0;
+  pdl_wait();  // the chunk counts
+  pdl_trigger();
   for (int base = 0; base < n; base += blockDim.x) {
     const int i = base + static_cast<int>(threadIdx.x);
     const int x = i < n ? chunk_cnt[i] : 0;
@@ -154,6 +159,7 @@ __global__ void __launch_bounds__(kCsrThreads)
   const int b = blockIdx.y, ch = blockIdx.x;
   const int v0 = ch * kCsrChunk, v1 = min(V, v0 + kCsrChunk);
   const T* row = reps + static_cast<size_t>(b) * V;
+  pdl_wait();  // the scanned chunk offsets
   int pos = chunk_off[static_cast<size_t>(b) * nchunks + ch];
   for (int base0 = v0; base0 < v1; base0 += kCsrThreads * kTileU) {
     const int base = base0 + warp * 32 * kTileU;
@@ -213,6 +219,7 @@ __global__ void __launch_bounds__(kTopkThreads)
   const int part = (((V + P - 1) / P) + 31) & ~31;
   const int v_lo = min(V, c * part), v_hi = min(V, v_lo + part);
   constexpr int kBits = Key<T>::kBits;
+  constexpr uint32_t kZeroKey = 1u << (kBits - 1);  // key of +0.0
   // Each warp takes kTileU*32 consecutive entries per step (entry
   // base + u*32 + lane), all kTileU loads of a lane issued first.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -235,8 +242,10 @@ __global__ void __launch_bounds__(kTopkThreads)
   for (int shift = kBits - 8; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
     __syncthreads();
-    // Warp-aggregated counts: most entries of a SPLADE row share one value
-    // (0), so the lanes with the same digit add once.
+    // Most entries of a SPLADE row are 0: when the key of 0.0 is still in the
+    // prefix group, its digit is the common one, otherwise lane 0's.
+    const bool zero_in_group = (kZeroKey & prefix_mask) == prefix;
+    const uint32_t zero_digit = (kZeroKey >> shift) & 0xFFu;
     for (int base = v_lo + warp * 32 * kTileU; base < v_hi; base += kStep) {
       uint32_t key[kTileU];
 #pragma unroll
@@ -249,8 +258,15 @@ __global__ void __launch_bounds__(kTopkThreads)
         const int v = base + u * 32 + lane;
         const uint32_t d =
             (v < v_hi && (key[u] & prefix_mask) == prefix) ? (key[u] >> shift) & 0xFFu : 256u;
-        const unsigned peers = __match_any_sync(0xFFFFFFFFu, d);
-        if (d < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
+        // The lanes holding the common digit add once (one ballot); the rest
+        // add one each.
+        const uint32_t dc = zero_in_group ? zero_digit : __shfl_sync(0xFFFFFFFFu, d, 0);
+        const unsigned same = __ballot_sync(0xFFFFFFFFu, d == dc);
+        if (d == dc) {
+          if (d < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[d], __popc(same));
+        } else if (d < 256u) {
+          atomicAdd(&hist[d], 1u);
+        }
       }
     }
     csync();  // every CTA's histogram is complete
@@ -379,14 +395,13 @@ int launch_csr_typed(const void* reps, int B, int V, float thr, int64_t* crow, i
                                                         nchunks, ws.chunk_cnt);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "csr_count_kernel launch");
-  csr_scan_kernel<<<1, 1024, 0, stream>>>(ws.chunk_cnt, B, nchunks, ws.chunk_off, crow);
-  e = cudaGetLastError();
+  e = launch_pdl(csr_scan_kernel, dim3(1), dim3(1024), 0, stream,
+                 static_cast<const int*>(ws.chunk_cnt), B, nchunks, ws.chunk_off, crow);
   if (e != cudaSuccess) return cuda_fail(e, "csr_scan_kernel launch");
   if (capacity > 0 && cols != nullptr && vals != nullptr) {
-    csr_fill_kernel<T><<<grid, kCsrThreads, 0, stream>>>(static_cast<const T*>(reps), V, thr,
-                                                         nchunks, ws.chunk_off, capacity, cols,
-                                                         static_cast<T*>(vals));
-    e = cudaGetLastError();
+    e = launch_pdl(csr_fill_kernel<T>, grid, dim3(kCsrThreads), 0, stream,
+                   static_cast<const T*>(reps), V, thr, nchunks,
+                   static_cast<const int*>(ws.chunk_off), capacity, cols, static_cast<T*>(vals));
     if (e != cudaSuccess) return cuda_fail(e, "csr_fill_kernel launch");
   }
   return SPARTON_OK;

@@ -30,7 +30,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _lib
-from .gemm import gemm, pad_to, round_up
+from .gemm import gemm, padded
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -144,14 +144,12 @@ class _Scores(torch.autograd.Function):
         ctx.shapes = (Bq, Bd, V)
         ctx.tc = q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and d.dtype == q.dtype
         if ctx.tc:
-            Vp, Bq8, Bd8 = round_up(V, 64), round_up(Bq, 8), round_up(Bd, 8)
-            qp, dp = pad_to(q, Bq8, Vp), pad_to(d, Bd8, Vp)
-            s = gemm(qp, dp, out_dtype=torch.float32)[:Bq, :Bd]
-            ctx.save_for_backward(qp, dp)
+            qv, dv = padded(q), padded(d)  # rows of round_up(V, 64), zero padding
+            s = gemm(qv, dv, out_dtype=torch.float32)
+            ctx.save_for_backward(qv, dv)
         else:
             s = torch.matmul(q.float(), d.float().t())
             ctx.save_for_backward(q, d)
-        s = s.contiguous()
         if group is not None:
             dist.all_reduce(s, op=dist.ReduceOp.SUM, group=group)
         return s
@@ -165,10 +163,10 @@ class _Scores(torch.autograd.Function):
             gq = (gs @ d.float()).to(q.dtype) if need_q else None
             gd = (gs.t() @ q.float()).to(d.dtype) if need_d else None
             return gq, gd, None
-        qp, dp = ctx.saved_tensors
-        gsp = pad_to(gs.to(qp.dtype), qp.shape[0], dp.shape[0])  # [Bq8, Bd8]
-        gq = gemm(gsp, dp, b_t=True)[:Bq, :V] if need_q else None        # gs @ d
-        gd = gemm(gsp, qp, a_t=True, b_t=True)[:Bd, :V] if need_d else None  # gs.T @ q
+        qv, dv = ctx.saved_tensors
+        gsv = padded(gs.to(qv.dtype), 8)                     # [Bq, Bd], rows of round_up(Bd, 8)
+        gq = gemm(gsv, dv, b_t=True) if need_q else None           # gs @ d   -> [Bq, V]
+        gd = gemm(gsv, qv, a_t=True, b_t=True) if need_d else None  # gs.T @ q -> [Bd, V]
         return gq, gd, None
 
 

@@ -152,8 +152,11 @@ def test_noalloc_checks_arguments_before_the_device(lib):
 def test_gemm_rejects_unaligned_operands(lib):
     """The tensor-core GEMM needs 16-byte operand rows (TMA): a K-major operand
     with K = 30522 (the vocabulary) is refused before any device work."""
-    st = lib.sparton_gemm(None, 0, None, 0, None, 2, 128, 128, 30522, None, 0, 128, None, 0, None)
+    st = lib.sparton_gemm(None, 0, 0, None, 0, 0, None, 2, 128, 128, 30522, None, 0, 128, None, 0,
+                          None)
     assert st == _lib.ERR_UNSUPPORTED and "multiple of 8" in _lib.last_error()
-    assert lib.sparton_gemm(None, 0, None, 0, None, 0, 8, 8, 8, None, 0, 8, None, 0,
+    assert lib.sparton_gemm(None, 0, 0, None, 0, 0, None, 0, 8, 8, 8, None, 0, 8, None, 0,
                             None) == _lib.ERR_UNSUPPORTED  # fp32 operands: no tensor-core kind
+    assert lib.sparton_gemm(None, 0, 16, None, 0, 0, None, 2, 8, 8, 24, None, 0, 8, None, 0,
+                            None) == _lib.ERR_INVALID_ARGUMENT  # lda below K
     assert lib.sparton_gemm_workspace_size(128, 128, 30528) > 128 * 128 * 4  # split-K partials

@@ -30,7 +30,7 @@ def run_gemm(A, a_cols, B, b_cols, bias=None, out_dtype=None):
     b_mem = B.t().contiguous() if b_cols else B.contiguous()
     C = torch.empty(M, N, dtype=out_dtype, device=A.device)
     ws = torch.empty(lib.sparton_gemm_workspace_size(M, N, K), dtype=torch.uint8, device=A.device)
-    st = lib.sparton_gemm(a_mem.data_ptr(), int(a_cols), b_mem.data_ptr(), int(b_cols),
+    st = lib.sparton_gemm(a_mem.data_ptr(), int(a_cols), 0, b_mem.data_ptr(), int(b_cols), 0,
                           _lib.ptr(bias), _lib.DTYPE[dt], M, N, K, C.data_ptr(),
                           _lib.DTYPE[out_dtype], N, ws.data_ptr(), ws.numel(),
                           torch.cuda.current_stream().cuda_stream)
@@ -103,3 +103,50 @@ def test_gemm_split_k_with_bias_is_deterministic():
     assert torch.equal(C1, C2)
     check(C1, A, B, bias)
 
+
+
+@pytest.mark.parametrize("b_t", [False, True])
+def test_gemm_padded_operands_and_unaligned_output(b_t):
+    """Operands given as row-contiguous views of zero-padded buffers (rows of a
+    multiple of 8 elements, as sparton_pad_rows makes them) and an output whose
+    rows (N = 2999 elements) are not 16-byte aligned, stored through the
+    epilogue's staging tile."""
+    from sparton_b200.gemm import gemm, padded
+
+    M, N, K = 200, 2999, 130
+    gen = torch.Generator().manual_seed(9)
+    A = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    B = torch.randn(N, K, generator=gen).to(torch.bfloat16).cuda()
+    a = padded(A, 8)                      # [M, K] view, rows of 136
+    b = padded(B.t(), 8) if b_t else padded(B, 8)
+    assert a.stride(0) == 136 and not a.is_contiguous()
+    C = gemm(a, b, b_t=b_t)
+    torch.cuda.synchronize()
+    assert C.shape == (M, N) and C.is_contiguous()
+    check(C, A, B, None)
+
+
+def test_pad_rows_zero_fills():
+    from sparton_b200.gemm import padded
+
+    x = torch.randn(37, 2999, dtype=torch.float16, device="cuda")
+    v = padded(x, 64)
+    torch.cuda.synchronize()
+    assert v.stride(0) == 3008 and torch.equal(v, x)
+    full = torch.as_strided(v, (37, 3008), (3008, 1))
+    assert (full[:, 2999:] == 0).all()
+
+
+def test_gemm_wide_output_picks_balanced_tiles():
+    """M = 32768 rows x N = 768 (the transform's dense layer): enough tiles for
+    several rounds over the SMs, so the kernel picks a narrower tile width; the
+    result is the same product."""
+    M, N, K = 32768, 768, 768
+    gen = torch.Generator().manual_seed(11)
+    A = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    B = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    bias = torch.randn(N, generator=gen).to(torch.bfloat16).cuda()
+    C = run_gemm(A, False, B, False, bias=bias)
+    torch.cuda.synchronize()
+    check(C[:4096], A[:4096], B, bias)
+    check(C[-4096:], A[-4096:], B, bias)
