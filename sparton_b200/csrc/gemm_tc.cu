@@ -48,10 +48,8 @@ namespace {
 constexpr int kBM = 128;   // output rows per tile = MMA M = TMEM lanes
 constexpr int kBN = 256;   // output columns per tile = max MMA N
 constexpr int kBK = 64;    // k per stage: 128-byte rows
-constexpr int kStages = 4;
+constexpr int kMaxStages = 6;  // the ring holds p.stages stages (4, 5 or 6: see plan)
 constexpr int kABytes = kBM * kBK * 2;
-constexpr int kBBytes = kBN * kBK * 2;
-constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kBoxBytes = 64 * kBK * 2;  // one MN-major box: 64 rows x 64 k
 constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kNumAcc * kBN;
@@ -59,12 +57,15 @@ constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 
 constexpr int kBarFull = 0;
-constexpr int kBarEmpty = kBarFull + kStages;
-constexpr int kBarTFull = kBarEmpty + kStages;
+constexpr int kBarEmpty = kBarFull + kMaxStages;
+constexpr int kBarTFull = kBarEmpty + kMaxStages;
 constexpr int kBarTEmpty = kBarTFull + kNumAcc;
 constexpr int kBarDrain = kBarTEmpty + kNumAcc;
 constexpr int kNumBars = kBarDrain + 1;
-constexpr int kCtrlOffset = kStages * kStageBytes;
+// Stage ring: p.stages stages of kABytes + bn * 128 bytes each in kRingBytes
+// (4 x 48 KB at bn = 256, 5 x 40 KB at 192, 6 x 32 KB at 128).
+constexpr int kRingBytes = 200 * 1024;
+constexpr int kCtrlOffset = kRingBytes;
 constexpr int kTmemHolderOffset = kCtrlOffset + kNumBars * 8;
 constexpr int kAbortOffset = kTmemHolderOffset + 4;
 constexpr int kCtrlBytes = 256;
@@ -72,12 +73,18 @@ constexpr int kCtrlBytes = 256;
 // fp32 tile per epilogue warp, so a row is stored by consecutive lanes.
 constexpr int kStageTileOffset = kCtrlOffset + kCtrlBytes;
 constexpr int kStageTileBytes = kEpiWarps * 32 * 33 * 4;
-constexpr int kSmemBytes = kStageTileOffset + kStageTileBytes + 1024;
+// The tile's bias (<= kBN values of the 16-bit type), one copy per epilogue
+// warp, fetched before the warp waits for the accumulator.
+constexpr int kBiasOffset = kStageTileOffset + kStageTileBytes;
+constexpr int kBiasBytes = kEpiWarps * kBN * 2;
+constexpr int kSmemBytes = kBiasOffset + kBiasBytes + 1024;
 
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, splits, kb_per_split;
   int bn;             // output columns per tile: 256, 192 or 128 (a multiple of 64)
+  int stages;         // stages in the TMA -> MMA ring
+  int stage_bytes;    // kABytes + bn * 128
   long long units;
   const void* bias;   // [N] in the output's element type family (T), or NULL
   void* C;            // [M][ldc] of type O (splits == 1)
@@ -152,18 +159,18 @@ __device__ void run_producer(const GemmParams& p, const CUtensorMap* tmA, const 
         const uint32_t full = c.bar(kBarFull + stage);
         // out-of-range parts of a box are zero-filled and counted
         mbar_arrive_expect_tx(full, static_cast<uint32_t>(kABytes + p.bn * kBK * 2));
-        load_stage<kAmn, kBmn>(tmA, tmB, stage_base + stage * kStageBytes, full, up, kb, p.bn);
+        load_stage<kAmn, kBmn>(tmA, tmB, stage_base + stage * p.stage_bytes, full, up, kb, p.bn);
       }
       __syncwarp();
       issued_mask |= 1u << stage;
       issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-      if (++stage == kStages) {
+      if (++stage == p.stages) {
         stage = 0;
         phase ^= 1;
       }
     }
   }
-  for (int s = 0; s < kStages; ++s) {
+  for (int s = 0; s < p.stages; ++s) {
     if (!(issued_mask & (1u << s))) continue;
     const uint32_t par = (issued_parity >> s) & 1;
     const uint32_t bar = c.bar((ok ? kBarEmpty : kBarFull) + s);
@@ -212,7 +219,7 @@ __device__ void run_mma(const GemmParams& p, uint32_t stage_base, uint32_t tmem_
       }
       tc_fence_after_sync();
       if (elect_one()) {
-        const uint32_t a_addr = stage_base + stage * kStageBytes;
+        const uint32_t a_addr = stage_base + stage * p.stage_bytes;
         const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
@@ -222,7 +229,7 @@ __device__ void run_mma(const GemmParams& p, uint32_t stage_base, uint32_t tmem_
       }
       __syncwarp();
       issued = true;
-      if (++stage == kStages) {
+      if (++stage == p.stages) {
         stage = 0;
         phase ^= 1;
       }
@@ -285,7 +292,7 @@ __device__ __forceinline__ void store_chunk_staged(const GemmParams& p, float* t
 
 template <typename T, typename O>
 __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl& c, int warp,
-                             int lane, float* stage_tile) {
+                             int lane, float* stage_tile, T* sbias) {
   const int quad = warp & 3;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
   uint32_t tile = 0;
@@ -293,6 +300,21 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
     const UnitPos up = unit_pos(p, u);
     const int acc = tile % kNumAcc;
     const uint32_t aph = (tile / kNumAcc) & 1;
+    if (p.bias != nullptr && p.splits == 1) {
+      // this tile's bias into the warp's shared copy (8 values per lane)
+      const T* bsrc = static_cast<const T*>(p.bias) + up.n0;
+      const int nb = min(p.bn, p.N - up.n0);
+      __syncwarp();  // the previous tile's reads of sbias are done
+      const int j = lane * 8;
+      if (j < nb) {
+        if (p.vec_bias && j + 8 <= nb) {
+          *reinterpret_cast<uint4*>(sbias + j) = __ldg(reinterpret_cast<const uint4*>(bsrc + j));
+        } else {
+          for (int i = 0; i < 8 && j + i < nb; ++i) sbias[j + i] = bsrc[j + i];
+        }
+      }
+      __syncwarp();
+    }
     const bool got = mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
                                        SPARTON_DEV_TIMEOUT_EPILOGUE);
     if (!__all_sync(0xFFFFFFFFu, got)) break;
@@ -324,26 +346,10 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
         }
       } else {
         if (p.bias != nullptr) {
-          const T* bp = static_cast<const T*>(p.bias) + n;
-          if (p.vec_bias && cnt == 32) {
-            // 32 bias values in four 16-byte loads (the same for every lane)
+          const T* bp = sbias + 32 * ch;  // shared copy, the same address in every lane
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = __ldg(reinterpret_cast<const uint4*>(bp) + j);
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                T pair[2];
-                memcpy(pair, &ws[h], 4);
-                v[8 * j + 2 * h] += to_f32<T>(pair[0]);
-                v[8 * j + 2 * h + 1] += to_f32<T>(pair[1]);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < cnt) v[i] += to_f32<T>(bp[i]);
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i < cnt) v[i] += to_f32<T>(bp[i]);
         }
         if (p.vec_store) {
           if (row_ok) store_row_chunk<O>(p, m, n, v);
@@ -373,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kTmemHolderOffset);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(c.bar(kBarFull + s), 1);
       mbar_init(c.bar(kBarEmpty + s), 1);
     }
@@ -406,7 +412,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     run_epilogue<T, O>(p, tmem_base, c, warp, lane,
-                       reinterpret_cast<float*>(smem + kStageTileOffset) + (warp - 2) * 32 * 33);
+                       reinterpret_cast<float*>(smem + kStageTileOffset) + (warp - 2) * 32 * 33,
+                       reinterpret_cast<T*>(smem + kBiasOffset) + (warp - 2) * kBN);
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -509,6 +516,9 @@ int launch_typed(CUtensorMapDataType dt, const GemmArgs& a, cudaStream_t stream)
   p.K = a.K;
   plan(a.M, a.N, a.K, p.m_tiles, p.n_tiles, p.k_blocks, p.splits, p.kb_per_split, p.bn);
   p.units = static_cast<long long>(p.m_tiles) * p.n_tiles * p.splits;
+  p.stage_bytes = kABytes + p.bn * kBK * 2;
+  p.stages = kRingBytes / p.stage_bytes;
+  if (p.stages > kMaxStages) p.stages = kMaxStages;
   p.bias = a.bias;
   p.C = a.C;
   p.ldc = a.ldc;

@@ -39,26 +39,39 @@ constexpr int kCsrChunk = 4096;
 constexpr int kCsrThreads = 256;
 constexpr int kTopkThreads = 512;
 constexpr int kTileU = 8;  // entries per lane per step of a row walk
+constexpr size_t kTopkStageBudget = 200 * 1024;  // shared memory for a staged row part
 
 // Order-preserving unsigned key of an element (larger value -> larger key;
 // NaN above +inf, as torch.topk orders it) and its bit width.
 template <typename T>
 struct Key;
+// `of` reads global memory through the read-only path; `at` reads any
+// address (the row staged in shared memory).
 template <>
 struct Key<float> {
   static constexpr int kBits = 32;
+  __device__ static __forceinline__ uint32_t conv(uint32_t u) {
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
   __device__ static __forceinline__ uint32_t of(const float* p) {
     // The bits are loaded as an integer: no float-typed value carries a NaN.
-    const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return conv(__ldg(reinterpret_cast<const unsigned int*>(p)));
+  }
+  __device__ static __forceinline__ uint32_t at(const float* p) {
+    return conv(*reinterpret_cast<const unsigned int*>(p));
   }
 };
 template <typename T16>
 struct Key16 {
   static constexpr int kBits = 16;
-  __device__ static __forceinline__ uint32_t of(const T16* p) {
-    const uint32_t u = __ldg(reinterpret_cast<const unsigned short*>(p));
+  __device__ static __forceinline__ uint32_t conv(uint32_t u) {
     return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+  }
+  __device__ static __forceinline__ uint32_t of(const T16* p) {
+    return conv(__ldg(reinterpret_cast<const unsigned short*>(p)));
+  }
+  __device__ static __forceinline__ uint32_t at(const T16* p) {
+    return conv(*reinterpret_cast<const unsigned short*>(p));
   }
 };
 template <>
@@ -200,7 +213,9 @@ __global__ void __launch_bounds__(kCsrThreads)
 // A thread-block cluster of P CTAs per row (P = 1 .. 8); CTA c walks the vocab
 // range [c*part, (c+1)*part). Shared memory: hist[256], then k_pad (key, id)
 // pairs (used in CTA 0).
-template <typename T>
+// kStaged: the CTA first copies its part of the row into shared memory (after
+// the pair arrays) and every pass reads it there instead of from L2.
+template <typename T, bool kStaged>
 __global__ void __launch_bounds__(kTopkThreads)
     topk_kernel(const T* __restrict__ reps, int V, int k, int k_pad, T* __restrict__ out_vals,
                 int32_t* __restrict__ out_idx) {
@@ -208,6 +223,7 @@ __global__ void __launch_bounds__(kTopkThreads)
   uint32_t* hist = smem;            // [256]
   uint32_t* skey = smem + 256;      // [k_pad]
   int32_t* sid = reinterpret_cast<int32_t*>(skey + k_pad);  // [k_pad]
+  T* srow = reinterpret_cast<T*>(sid + k_pad);              // [part] when kStaged
   __shared__ int tmp[32];
   __shared__ uint32_t s_prefix, s_remaining, s_eq_before, s_gt;
   namespace cg = cooperative_groups;
@@ -218,6 +234,14 @@ __global__ void __launch_bounds__(kTopkThreads)
   const T* row = reps + static_cast<size_t>(b) * V;
   const int part = (((V + P - 1) / P) + 31) & ~31;
   const int v_lo = min(V, c * part), v_hi = min(V, v_lo + part);
+  if (kStaged) {
+    for (int i = threadIdx.x; i < v_hi - v_lo; i += kTopkThreads) srow[i] = row[v_lo + i];
+    __syncthreads();
+  }
+  // the key of vocab id v of this CTA's part
+  auto key_of = [&](int v) -> uint32_t {
+    return kStaged ? Key<T>::at(srow + (v - v_lo)) : Key<T>::of(row + v);
+  };
   constexpr int kBits = Key<T>::kBits;
   constexpr uint32_t kZeroKey = 1u << (kBits - 1);  // key of +0.0
   // Each warp takes kTileU*32 consecutive entries per step (entry
@@ -251,7 +275,7 @@ __global__ void __launch_bounds__(kTopkThreads)
 #pragma unroll
       for (int u = 0; u < kTileU; ++u) {
         const int v = base + u * 32 + lane;
-        key[u] = v < v_hi ? Key<T>::of(row + v) : 0u;
+        key[u] = v < v_hi ? key_of(v) : 0u;
       }
 #pragma unroll
       for (int u = 0; u < kTileU; ++u) {
@@ -314,7 +338,7 @@ __global__ void __launch_bounds__(kTopkThreads)
 #pragma unroll
     for (int u = 0; u < kTileU; ++u) {
       const int v = base + u * 32 + lane;
-      key[u] = v < v_hi ? Key<T>::of(row + v) : 0u;
+      key[u] = v < v_hi ? key_of(v) : 0u;
     }
     unsigned eqm[kTileU];
     int warp_eq = 0;
@@ -413,13 +437,7 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
   if (B == 0 || k == 0) return SPARTON_OK;
   int k_pad = 1;
   while (k_pad < k) k_pad <<= 1;
-  const size_t smem = (256 + 2 * static_cast<size_t>(k_pad)) * sizeof(uint32_t);
-  if (smem > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute(topk_kernel<T>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(topk_kernel)");
-  }
+  const size_t smem_pairs = (256 + 2 * static_cast<size_t>(k_pad)) * sizeof(uint32_t);
   // Enough CTAs for two per SM, each walking at least 16384 entries of its
   // row (shorter spans lose more to the cluster barriers than they gain:
   // [128, 30522] ran 50 µs with one CTA per row, 59 µs with two).
@@ -430,7 +448,6 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(P), static_cast<unsigned>(B));
   cfg.blockDim = dim3(kTopkThreads);
-  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -439,12 +456,34 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (P > 1 && !cluster_fits(topk_kernel<T>, &cfg, P, smem)) {
-    cfg.gridDim = dim3(1u, static_cast<unsigned>(B));
-    attr[0].val.clusterDim.x = 1;
+  // Stage the CTA's part of the row in shared memory when it fits (config 2:
+  // 61 KB of a 30522-wide bf16 row; config 3: 62 KB per CTA of an 8-CTA cluster).
+  auto plan_smem = [&](int p) {
+    const size_t part = static_cast<size_t>((((V + p - 1) / p) + 31) & ~31);
+    const size_t staged = smem_pairs + part * sizeof(T);
+    return staged <= kTopkStageBudget ? staged : 0;
+  };
+  auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(
+          kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+    }
+    cfg.dynamicSmemBytes = smem;
+    if (P > 1 && !cluster_fits(kernel, &cfg, P, smem)) {
+      P = 1;
+      cfg.gridDim = dim3(1u, static_cast<unsigned>(B));
+      attr[0].val.clusterDim.x = 1;
+      return cudaErrorNotReady;  // re-plan the shared memory for one CTA per row
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(reps), V, k, k_pad,
+                              static_cast<T*>(vals), idx);
+  };
+  cudaError_t e = cudaErrorNotReady;
+  for (int attempt = 0; attempt < 2 && e == cudaErrorNotReady; ++attempt) {
+    const size_t staged = plan_smem(P);
+    e = staged ? launch(topk_kernel<T, true>, staged) : launch(topk_kernel<T, false>, smem_pairs);
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel<T>, static_cast<const T*>(reps), V,
-                                           k, k_pad, static_cast<T*>(vals), idx);
   if (e != cudaSuccess) return cuda_fail(e, "topk_kernel launch");
   return SPARTON_OK;
 }
