@@ -87,6 +87,7 @@ typedef enum {
 #define SPARTON_DEV_TIMEOUT_DRAIN 0x104u
 #define SPARTON_DEV_TIMEOUT_SELFTEST 0x1F0u /* sparton_selftest_wait_timeout only */
 #define SPARTON_DEV_TIMEOUT_PEER 0x105u     /* sparton_hidden_allreduce: a peer never signalled */
+#define SPARTON_DEV_TIMEOUT_SCAN 0x106u     /* sparton_reps_csr: a chunk count never arrived */
 
 int sparton_abi_version(void);
 

@@ -8,16 +8,20 @@
 //   flops_regularization (:85-87) = mean_v (sum_b reps[b, v])^2
 // Here reg_fwd_kernel reads reps once and produces the column sums
 // colsum[v] = sum_b reps[b, v] (kept for the backward) and, per block, the
-// partial sums of |reps| and of colsum^2; reg_total_kernel adds the block
-// partials in a fixed order (deterministic) and scales them, giving
+// partial sums of |reps| and of colsum^2; the last block to finish (a ticket
+// counter in the workspace, zeroed before the launch) adds the block partials
+// in a fixed order (deterministic) and scales them, giving
 // out = {scale_l1 * sum |reps|, scale_flops * sum_v colsum^2} (1/B and 1/V for
 // the losses; shards' outputs then simply add up). reg_bwd_kernel writes
 //   grad[b, v] = g_l1 * scale_l1 * sign(reps[b, v]) + g_flops * scale_flops * colsum[v]
-// with the upstream gradients g_l1, g_flops read from device memory (1/B and
-// 2/V as scales), so neither direction needs a host round trip or any
-// arithmetic outside the kernels.
+// elementwise over the flattened [B * V] (16-byte loads and stores), with the
+// upstream gradients g_l1, g_flops read from device memory (1/B and 2/V as
+// scales), so neither direction needs a host round trip or any arithmetic
+// outside the kernels.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "dtype.cuh"
 #include "internal.h"
@@ -26,40 +30,88 @@ namespace sparton {
 namespace {
 
 constexpr int kRegWarps = 8;  // rows are strided over the warps of a block
-constexpr int kTotalThreads = 1024;
+constexpr int kRowUnroll = 8;  // row loads of a lane in flight
 
-// One block per 32 vocabulary columns (one per lane); warp w sums rows
-// b = w, w + 8, ... of its lane's column.
-template <typename T>
+// kC consecutive columns of a row as fp32 (one 2 * sizeof(T)-byte load for kC = 2).
+template <typename T, int kC>
+__device__ __forceinline__ void load_cols(const T* p, float (&x)[kC]) {
+  if constexpr (kC == 1) {
+    x[0] = ldg_f32<T>(p);
+  } else if constexpr (sizeof(T) == 2) {
+    const unsigned int w = __ldg(reinterpret_cast<const unsigned int*>(p));
+    const T* e = reinterpret_cast<const T*>(&w);
+    x[0] = to_f32<T>(e[0]);
+    x[1] = to_f32<T>(e[1]);
+  } else {
+    const float2 w = __ldg(reinterpret_cast<const float2*>(p));
+    x[0] = w.x;
+    x[1] = w.y;
+  }
+}
+
+// One block per 32 * kC vocabulary columns (kC per lane: kC = 2 when V is
+// even and reps is aligned for the pair loads); warp w sums rows b = w, w + 8,
+// ... of its lane's columns, kRowUnroll loads in flight. The block's partials
+// of |reps| and colsum^2 go to partials[2 * block]; the last block adds them
+// over the blocks in order and writes the scaled totals, then re-arms the
+// ticket counter.
+template <typename T, int kC>
 __global__ void __launch_bounds__(kRegWarps * 32)
     reg_fwd_kernel(const T* __restrict__ reps, int B, int V, float* __restrict__ colsum,
-                   float* __restrict__ partials) {
-  __shared__ float s_col[kRegWarps][32];
+                   float* __restrict__ partials, unsigned int* __restrict__ counter,
+                   float scale_l1, float scale_flops, float* __restrict__ totals) {
+  __shared__ float s_col[kRegWarps][32 * kC];
   __shared__ float s_abs[kRegWarps][32];
+  __shared__ bool s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_trigger();
-  const int v = blockIdx.x * 32 + lane;
-  float col = 0.f, ab = 0.f;
-  if (v < V) {
-#pragma unroll 8
-    for (int b = warp; b < B; b += kRegWarps) {
-      const float x = ldg_f32<T>(reps + static_cast<size_t>(b) * V + v);
-      col += x;
-      ab += fabsf(x);
+  const int v0 = (blockIdx.x * 32 + lane) * kC;
+  float col[kC], ab = 0.f;
+#pragma unroll
+  for (int j = 0; j < kC; ++j) col[j] = 0.f;
+  if (v0 < V) {
+    const T* p = reps + v0;
+    int b = warp;
+    for (; b + (kRowUnroll - 1) * kRegWarps < B; b += kRowUnroll * kRegWarps) {
+      float x[kRowUnroll][kC];
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u)
+        load_cols<T, kC>(p + static_cast<size_t>(b + u * kRegWarps) * V, x[u]);
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u)
+#pragma unroll
+        for (int j = 0; j < kC; ++j) {
+          col[j] += x[u][j];
+          ab += fabsf(x[u][j]);
+        }
+    }
+    for (; b < B; b += kRegWarps) {
+      float x[kC];
+      load_cols<T, kC>(p + static_cast<size_t>(b) * V, x);
+#pragma unroll
+      for (int j = 0; j < kC; ++j) {
+        col[j] += x[j];
+        ab += fabsf(x[j]);
+      }
     }
   }
-  s_col[warp][lane] = col;
+#pragma unroll
+  for (int j = 0; j < kC; ++j) s_col[warp][lane * kC + j] = col[j];
   s_abs[warp][lane] = ab;
   __syncthreads();
   if (warp == 0) {
-    float c = 0.f, a = 0.f;
+    float a = 0.f, sq = 0.f;
 #pragma unroll
-    for (int w = 0; w < kRegWarps; ++w) {
-      c += s_col[w][lane];
-      a += s_abs[w][lane];
+    for (int w = 0; w < kRegWarps; ++w) a += s_abs[w][lane];
+#pragma unroll
+    for (int j = 0; j < kC; ++j) {
+      float c = 0.f;
+#pragma unroll
+      for (int w = 0; w < kRegWarps; ++w) c += s_col[w][lane * kC + j];
+      if (v0 + j < V) {
+        colsum[v0 + j] = c;
+        sq += c * c;
+      }
     }
-    if (v < V) colsum[v] = c;
-    float sq = v < V ? c * c : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
@@ -68,88 +120,130 @@ __global__ void __launch_bounds__(kRegWarps * 32)
     if (lane == 0) {
       partials[2 * blockIdx.x] = a;
       partials[2 * blockIdx.x + 1] = sq;
+      __threadfence();  // the partials before the ticket
+      s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
     }
   }
-}
-
-// One block: out[k] = scale_k * sum over blocks of partials[2*blk + k], in a
-// fixed order.
-__global__ void __launch_bounds__(kTotalThreads)
-    reg_total_kernel(const float* __restrict__ partials, int nblocks, float scale_l1,
-                     float scale_flops, float* __restrict__ totals) {
-  __shared__ float s[2][kTotalThreads / 32];
-  pdl_wait();  // the block partials
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // every block's partials are visible
+  const int nblocks = static_cast<int>(gridDim.x);
   float a = 0.f, q = 0.f;
-  for (int i = threadIdx.x; i < nblocks; i += kTotalThreads) {
-    a += partials[2 * i];
-    q += partials[2 * i + 1];
+  for (int i = threadIdx.x; i < nblocks; i += kRegWarps * 32) {
+    a += __ldcg(partials + 2 * i);
+    q += __ldcg(partials + 2 * i + 1);
   }
+#pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
     q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // s_abs / s_col reads are done
   if (lane == 0) {
-    s[0][warp] = a;
-    s[1][warp] = q;
+    s_abs[0][warp] = a;
+    s_abs[1][warp] = q;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float ta = 0.f, tq = 0.f;
-    for (int w = 0; w < kTotalThreads / 32; ++w) {
-      ta += s[0][w];
-      tq += s[1][w];
+    for (int w = 0; w < kRegWarps; ++w) {
+      ta += s_abs[0][w];
+      tq += s_abs[1][w];
     }
     totals[0] = ta * scale_l1;
     totals[1] = tq * scale_flops;
+    *counter = 0u;
   }
 }
 
-// Thread per column v (coalesced along a row); rows b = blockIdx.y, + gridDim.y, ...
-template <typename T>
+// grad over the flattened [B * V]: kPer consecutive elements per thread and
+// step (16-byte loads and stores when reps and grad are 16-byte aligned, else
+// kPer = 1); the column index advances with the element and wraps at V.
+template <typename T, int kPer>
 __global__ void __launch_bounds__(256)
     reg_bwd_kernel(const T* __restrict__ reps, const float* __restrict__ colsum,
                    const float* __restrict__ g_l1, const float* __restrict__ g_flops,
-                   float scale_l1, float scale_flops, int B, int V, T* __restrict__ grad) {
-  const int v = blockIdx.x * blockDim.x + threadIdx.x;
-  if (v >= V) return;
+                   float scale_l1, float scale_flops, long long n, int V, T* __restrict__ grad) {
   const float c0 = g_l1 != nullptr ? __ldg(g_l1) * scale_l1 : 0.f;
   const float c1 = g_flops != nullptr ? __ldg(g_flops) * scale_flops : 0.f;
-  const float cv = c1 * __ldg(colsum + v);
-  for (int b = blockIdx.y; b < B; b += gridDim.y) {
-    const size_t i = static_cast<size_t>(b) * V + v;
-    const float x = ldg_f32<T>(reps + i);
+  const long long nvec = n / kPer;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long vi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; vi < nvec;
+       vi += stride) {
+    const long long g = vi * kPer;
+    int v = static_cast<int>(g % V);
+    if constexpr (kPer == 1) {
+      const float x = ldg_f32<T>(reps + g);
+      const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+      grad[g] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
+    } else {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(reps + g));
+      const T* e = reinterpret_cast<const T*>(&w);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const float x = to_f32<T>(e[i]);
+        const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+        oe[i] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
+        if (++v == V) v = 0;
+      }
+      *reinterpret_cast<uint4*>(grad + g) = o;
+    }
+  }
+  // the last n % kPer elements
+  const long long t = nvec * kPer + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (kPer > 1 && t < n && blockIdx.x == 0) {
+    const float x = ldg_f32<T>(reps + t);
     const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-    grad[i] = from_f32<T>(fmaf(c0, s, cv));
+    grad[t] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + static_cast<int>(t % V))));
   }
 }
 
+int fwd_blocks(int V, int kc) { return (V + 32 * kc - 1) / (32 * kc); }
+
 template <typename T>
 int launch_fwd_typed(const void* reps, int B, int V, float scale_l1, float scale_flops,
-                     float* colsum, float* totals, float* partials, cudaStream_t stream) {
-  const int nblocks = (V + 31) / 32;
-  reg_fwd_kernel<T><<<nblocks, kRegWarps * 32, 0, stream>>>(static_cast<const T*>(reps), B, V,
-                                                            colsum, partials);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "reg_fwd_kernel launch");
-  e = launch_pdl(reg_total_kernel, dim3(1), dim3(kTotalThreads), 0, stream,
-                 static_cast<const float*>(partials), nblocks, scale_l1, scale_flops, totals);
-  if (e != cudaSuccess) return cuda_fail(e, "reg_total_kernel launch");
-  return SPARTON_OK;
+                     float* colsum, float* totals, void* workspace, cudaStream_t stream) {
+  unsigned int* counter = static_cast<unsigned int*>(workspace);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(reg counter)");
+  const bool pairs =
+      V % 2 == 0 && reinterpret_cast<uintptr_t>(reps) % (2 * sizeof(T)) == 0;
+  if (pairs)
+    reg_fwd_kernel<T, 2><<<fwd_blocks(V, 2), kRegWarps * 32, 0, stream>>>(
+        static_cast<const T*>(reps), B, V, colsum, partials, counter, scale_l1, scale_flops,
+        totals);
+  else
+    reg_fwd_kernel<T, 1><<<fwd_blocks(V, 1), kRegWarps * 32, 0, stream>>>(
+        static_cast<const T*>(reps), B, V, colsum, partials, counter, scale_l1, scale_flops,
+        totals);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "reg_fwd_kernel launch");
 }
 
 template <typename T>
 int launch_bwd_typed(const void* reps, const float* colsum, const float* g_l1,
                      const float* g_flops, float scale_l1, float scale_flops, int B, int V,
                      void* grad, cudaStream_t stream) {
-  const unsigned cols = static_cast<unsigned>((V + 255) / 256);
-  // Enough blocks for ~8 per SM, each covering a strided subset of the rows.
-  unsigned rows = static_cast<unsigned>((8ll * device_sm_count() + cols - 1) / cols);
-  if (rows > static_cast<unsigned>(B)) rows = static_cast<unsigned>(B);
-  if (rows < 1) rows = 1;
-  reg_bwd_kernel<T><<<dim3(cols, rows), 256, 0, stream>>>(
-      static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, B, V,
-      static_cast<T*>(grad));
+  const long long n = static_cast<long long>(B) * V;
+  if (n == 0) return SPARTON_OK;
+  constexpr int kPer = 16 / sizeof(T);
+  const bool vec = reinterpret_cast<uintptr_t>(reps) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(grad) % 16 == 0;
+  const long long units = vec ? n / kPer : n;
+  // at most 16 blocks per SM; every thread takes a few vectors
+  const long long blocks =
+      std::max(1ll, std::min((units + 255) / 256, 16ll * device_sm_count()));
+  if (vec)
+    reg_bwd_kernel<T, kPer><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, n, V,
+        static_cast<T*>(grad));
+  else
+    reg_bwd_kernel<T, 1><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, n, V,
+        static_cast<T*>(grad));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reg_bwd_kernel launch");
   return SPARTON_OK;
@@ -157,20 +251,22 @@ int launch_bwd_typed(const void* reps, const float* colsum, const float* g_l1,
 
 }  // namespace
 
-size_t reg_workspace_bytes(int64_t V) { return align256(static_cast<size_t>((V + 31) / 32) * 8); }
+// [0, 256): the ticket counter; then the blocks' partials (2 floats each).
+size_t reg_workspace_bytes(int64_t V) {
+  return 256 + align256(static_cast<size_t>((V + 31) / 32) * 8);
+}
 
 int launch_reg_fwd(int dtype, const void* reps, int B, int V, float scale_l1, float scale_flops,
                    float* colsum, float* totals, void* workspace, cudaStream_t stream) {
-  float* partials = static_cast<float*>(workspace);
   switch (dtype) {
     case SPARTON_DTYPE_BF16:
       return launch_fwd_typed<__nv_bfloat16>(reps, B, V, scale_l1, scale_flops, colsum, totals,
-                                             partials, stream);
+                                             workspace, stream);
     case SPARTON_DTYPE_F16:
-      return launch_fwd_typed<__half>(reps, B, V, scale_l1, scale_flops, colsum, totals, partials,
+      return launch_fwd_typed<__half>(reps, B, V, scale_l1, scale_flops, colsum, totals, workspace,
                                       stream);
     case SPARTON_DTYPE_F32:
-      return launch_fwd_typed<float>(reps, B, V, scale_l1, scale_flops, colsum, totals, partials,
+      return launch_fwd_typed<float>(reps, B, V, scale_l1, scale_flops, colsum, totals, workspace,
                                      stream);
     default:
       return fail(SPARTON_ERR_UNSUPPORTED, "unknown dtype %d", dtype);

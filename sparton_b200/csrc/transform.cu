@@ -1,6 +1,6 @@
 // transform.cu — the MLM transform in front of the head, GELU + LayerNorm part:
 //   h = LayerNorm(gelu(y)) * gamma + beta,   y = x @ Wd^T + bd (the dense layer,
-//   a plain GEMM left to cuBLAS)
+//   the tcgen05 GEMM of gemm_tc.cu)
 // as in hhkbble/sparton training/model.py:25-35 (RoBERTa: dense, gelu,
 // layer_norm) and BERT's predictions.transform (model.py:14-19), whose output
 // is the head's input (model.py:82-85). gelu is the exact erf form
@@ -11,19 +11,21 @@
 //                            rstd = 1/sqrt(var + eps) (biased variance, as
 //                            torch's LayerNorm), h = (g - mean) * rstd * gamma
 //                            + beta in the input dtype; mean / rstd saved
-//   transform_bwd_row_kernel one warp per row, from dh (the head's d_hidden):
+//   transform_bwd_fused_kernel (D % 8 == 0, D <= 1024) one warp per row, from
+//                            dh (the head's d_hidden):
 //                            xh = (g - mean) * rstd, dxh = dh * gamma,
 //                            dg = rstd * (dxh - mean(dxh) - xh * mean(dxh * xh)),
-//                            dy = dg * gelu'(y)
-//   transform_bwd_col8_kernel 256 columns (8 per lane, D % 8 == 0; else
-//                            transform_bwd_col_kernel, 32) x a block of rows per
-//                            CTA: partial sums of dh * xh (d_gamma), dh (d_beta)
-//                            and dy (d_bd)
+//                            dy = dg * gelu'(y); and per CTA the column sums
+//                            of dh * xh (d_gamma), dh (d_beta), dy (d_bd)
+//   transform_bwd_row_kernel, transform_bwd_col_kernel  the same in two
+//                            kernels for other D (rows of any length)
 //   transform_col_reduce     the partials in a fixed order -> d_gamma, d_beta,
 //                            d_bd (deterministic, no atomics)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
+
+#include <algorithm>
 
 #include <type_traits>
 
@@ -254,6 +256,95 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   }
 }
 
+// D % 8 == 0, D <= 256 * kNv: the row pass and the column partial sums in one
+// kernel. CTA c takes the rows [c * rows / grid, (c + 1) * rows / grid), warp
+// w every eighth of them from the w-th; lane l owns the 8-column chunks l,
+// l + 32, ... One erff and one expf per element: the first pass keeps (dh,
+// xh, gelu'(y)) of each element in registers, the second writes dy and adds
+// dh * xh, dh and the rounded dy into the warp's column sums in shared memory
+// (each lane its own columns: no conflicts, no atomics). The CTA then adds
+// its warps' sums in warp order into partials[c][k][col] (k = gamma, beta,
+// bias) when partials is not NULL. The grid depends on rows only, so the
+// column sums are deterministic.
+template <typename T, int kNv>
+__global__ void __launch_bounds__(kRowWarps * 32, 2)
+    transform_bwd_fused_kernel(const T* __restrict__ dh, const T* __restrict__ y,
+                               const T* __restrict__ gamma, const float* __restrict__ mean,
+                               const float* __restrict__ rstd, int rows, int D,
+                               T* __restrict__ dy, float* __restrict__ partials) {
+  extern __shared__ float sh[];
+  float* sgamma = sh;                                     // [D]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* acc = sh + D + static_cast<size_t>(warp) * 3 * D;  // this warp's [3][D]
+  const bool want = partials != nullptr;
+  for (int i = threadIdx.x; i < D; i += kRowWarps * 32) sgamma[i] = to_f32<T>(gamma[i]);
+  if (want)
+    for (int i = lane; i < 3 * D; i += 32) acc[i] = 0.f;
+  __syncthreads();
+  const long long r_lo = static_cast<long long>(blockIdx.x) * rows / gridDim.x;
+  const long long r_hi = static_cast<long long>(blockIdx.x + 1) * rows / gridDim.x;
+  const float inv_d = 1.f / static_cast<float>(D);
+  for (long long r = r_lo + warp; r < r_hi; r += kRowWarps) {
+    const size_t o = static_cast<size_t>(r) * D;
+    const float mu = mean[r], rs = rstd[r];
+    float gv[kNv][8], xh[kNv][8], gp[kNv][8];
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNv; ++j) {
+      const int d = 8 * (lane + 32 * j);
+      if (d < D) {
+        float yv[8];
+        load8<T>(y + o + d, yv);
+        load8<T>(dh + o + d, gv[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float e = erff(yv[i] * 0.70710678118654752f);
+          // gelu rounded to T, and d gelu / dy = Phi(y) + y * phi(y)
+          const float g = to_f32<T>(from_f32<T>(0.5f * yv[i] * (1.f + e)));
+          gp[j][i] = 0.5f * (1.f + e) + yv[i] * 0.39894228040143268f * expf(-0.5f * yv[i] * yv[i]);
+          xh[j][i] = (g - mu) * rs;
+          const float dxh = gv[j][i] * sgamma[d + i];
+          a += dxh;
+          b += dxh * xh[j][i];
+        }
+      }
+    }
+    a = warp_sum(a) * inv_d;
+    b = warp_sum(b) * inv_d;
+#pragma unroll
+    for (int j = 0; j < kNv; ++j) {
+      const int d = 8 * (lane + 32 * j);
+      if (d < D) {
+        float out[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          out[i] = rs * (gv[j][i] * sgamma[d + i] - a - xh[j][i] * b) * gp[j][i];
+        store8<T>(dy + o + d, out);
+        if (want) {
+          float* pg = acc + d;
+          float* pb = acc + D + d;
+          float* pd = acc + 2 * D + d;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pg[i] += gv[j][i] * xh[j][i];
+            pb[i] += gv[j][i];
+            pd[i] += to_f32<T>(from_f32<T>(out[i]));
+          }
+        }
+      }
+    }
+  }
+  if (!want) return;
+  __syncthreads();
+  const float* all = sh + D;
+  for (int c = threadIdx.x; c < 3 * D; c += kRowWarps * 32) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRowWarps; ++w) t += all[static_cast<size_t>(w) * 3 * D + c];
+    partials[static_cast<size_t>(blockIdx.x) * 3 * D + c] = t;
+  }
+}
+
 // CTA (column block cx of 32, row block ry of kColRows): lane = column, the 8
 // warps stride the rows; partials[ry][k][col] for k = gamma, beta, bias.
 template <typename T>
@@ -378,10 +469,45 @@ int fwd_typed(const void* y, const void* gamma, const void* beta, float eps, int
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "transform_fwd_kernel launch");
 }
 
+// CTAs of transform_bwd_fused_kernel: two per SM of a B200 (a constant, so the
+// column sums' order depends on the shape only), at least 8 rows each.
+constexpr int kFusedCtas = 2 * 148;
+int fused_grid(int rows) { return std::max(1, std::min(kFusedCtas, (rows + 7) / 8)); }
+size_t fused_smem(int D) { return (static_cast<size_t>(D) + kRowWarps * 3 * D) * sizeof(float); }
+
+template <typename T, int kNv>
+int bwd_fused(const void* dh, const void* y, const void* gamma, const float* mean,
+              const float* rstd, int rows, int D, void* dy, void* d_gamma, void* d_beta,
+              void* d_bias, float* partials, cudaStream_t stream) {
+  const bool params = d_gamma != nullptr || d_beta != nullptr || d_bias != nullptr;
+  const int grid = fused_grid(rows);
+  const size_t smem = fused_smem(D);
+  auto kernel = transform_bwd_fused_kernel<T, kNv>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_fail(e, "transform_bwd_fused_kernel smem");
+  kernel<<<grid, kRowWarps * 32, smem, stream>>>(
+      static_cast<const T*>(dh), static_cast<const T*>(y), static_cast<const T*>(gamma), mean, rstd,
+      rows, D, static_cast<T*>(dy), params ? partials : nullptr);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "transform_bwd_fused_kernel launch");
+  if (!params) return SPARTON_OK;
+  transform_col_reduce<T><<<(D + 255) / 256, 256, 0, stream>>>(
+      partials, grid, D, static_cast<T*>(d_gamma), static_cast<T*>(d_beta), static_cast<T*>(d_bias));
+  e = cudaGetLastError();
+  return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "transform_col_reduce launch");
+}
+
 template <typename T>
 int bwd_typed(const void* dh, const void* y, const void* gamma, const float* mean,
               const float* rstd, int rows, int D, void* dy, void* d_gamma, void* d_beta,
               void* d_bias, float* partials, cudaStream_t stream) {
+  if (vec_path(D)) {
+    const int nv = (D + 255) / 256;
+    auto f = nv == 1 ? bwd_fused<T, 1> : nv == 2 ? bwd_fused<T, 2> : nv == 3 ? bwd_fused<T, 3>
+                                                                             : bwd_fused<T, 4>;
+    return f(dh, y, gamma, mean, rstd, rows, D, dy, d_gamma, d_beta, d_bias, partials, stream);
+  }
   const unsigned grid = static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps);
   auto go = [&](auto kernel) {
     kernel<<<grid, kRowWarps * 32, 0, stream>>>(static_cast<const T*>(dh), static_cast<const T*>(y),
@@ -418,7 +544,9 @@ int bwd_typed(const void* dh, const void* y, const void* gamma, const float* mea
 }  // namespace
 
 size_t transform_workspace_bytes(int64_t rows, int64_t D) {
-  const int64_t nb = (rows + kColRows - 1) / kColRows;
+  int64_t nb = (rows + kColRows - 1) / kColRows;  // column kernels' row blocks
+  if (vec_path(static_cast<int>(D)))
+    nb = fused_grid(static_cast<int>(std::min<int64_t>(rows, 1 << 30)));
   return align256(static_cast<size_t>(nb > 0 ? nb : 1) * 3 * static_cast<size_t>(D) * sizeof(float));
 }
 

@@ -4,12 +4,13 @@ transform of BERT's ``cls.predictions`` and RoBERTa's ``lm_head``: dense →
 exact-erf gelu → LayerNorm) and ``ProjectionSparton`` (:65-85).
 
 * ``MLMTransform(dense, layer_norm)``: ``h = LayerNorm(gelu(dense(x)))`` with
-  the dense layer as a plain cuBLAS GEMM (``F.linear``) and gelu + LayerNorm in
-  one kernel (``sparton_transform_fwd``, csrc/transform.cu) that writes the
-  head's input and saves each row's mean / rstd; the backward is one row
-  kernel (d of LayerNorm and gelu) plus fixed-order column sums for
-  d_gamma / d_beta / d_dense_bias (``sparton_transform_bwd``) and two cuBLAS
-  GEMMs for d_x and d_dense_weight. Parameters are shared with the modules it
+  the dense layer on the library's tcgen05 GEMM (``sparton_gemm``, bias in its
+  epilogue; fp32 inputs stay on ``F.linear``) and gelu + LayerNorm in one
+  kernel (``sparton_transform_fwd``, csrc/transform.cu) that writes the head's
+  input and saves each row's mean / rstd; the backward is one kernel (d of
+  LayerNorm and gelu, and per-CTA column sums) plus a fixed-order reduction
+  for d_gamma / d_beta / d_dense_bias (``sparton_transform_bwd``) and two
+  tcgen05 GEMMs for d_x and d_dense_weight. Parameters are shared with the modules it
   is built from. ``MLMTransform.from_module(transform)`` accepts BERT's
   ``BertPredictionHeadTransform`` (``dense``, ``transform_act_fn``,
   ``LayerNorm``) and the reference's ``RobertaTransform`` (``dense``,

@@ -75,6 +75,41 @@ def test_edge_rows():
     check(reps, -1.0, [3])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_topk_list_and_row_paths(dtype):
+    """Rows whose candidates (entries at or above the k-th largest key's top
+    8 bits) overflow the shared-memory list take the row path: all-equal rows,
+    rows with fewer nonzeros than k (the k-th largest is 0), signed values;
+    and reps whose storage is not 16-byte aligned (scalar first pass)."""
+    B, V = 6, 30522
+    gen = torch.Generator().manual_seed(11)
+    reps = torch.zeros(B, V)
+    reps[0] = 1.0                                   # all equal: row path
+    reps[1, torch.randperm(V, generator=gen)[:100]] = torch.rand(100, generator=gen) + 0.5
+    reps[2] = splade_like(1, V, torch.float32, seed=12)[0]
+    reps[3] = torch.randn(V, generator=gen)         # negative and positive
+    reps[4, ::3] = 2.0                              # 10174 equals of the top value
+    reps[5] = splade_like(1, V, torch.float32, seed=13, zero_frac=0.9)[0]
+    reps = reps.to(dtype)
+    check(reps, 0.0, [1, 256, 4096])
+    # the same rows one element past a 16-byte boundary
+    flat = torch.zeros(B * V + 8, dtype=dtype)
+    flat[1:1 + B * V] = reps.reshape(-1)
+    view = flat.cuda()[1:1 + B * V].view(B, V)
+    assert view.data_ptr() % 16 != 0
+    x = reps.float().numpy()
+    for k in (1, 256, 4096):
+        v, i = sparse.topk_reps(view, k)
+        rv, ri = so.topk(x, k)
+        np.testing.assert_array_equal(v.float().cpu().numpy(), rv)
+        np.testing.assert_array_equal(i.cpu().numpy(), ri)
+    crow, cols, vals = sparse.csr_arrays(view, 0.0)
+    rc, cc, vc = so.csr(x, 0.0)
+    np.testing.assert_array_equal(crow.cpu().numpy(), rc)
+    np.testing.assert_array_equal(cols.cpu().numpy(), cc)
+    np.testing.assert_array_equal(vals.float().cpu().numpy(), vc)
+
+
 def test_k_zero_and_empty():
     reps = splade_like(3, 100, torch.bfloat16, seed=1).cuda()
     v, i = sparse.topk_reps(reps, 0)
