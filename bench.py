@@ -408,7 +408,7 @@ def run_losses(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
     pair = torch.empty(2, dtype=torch.float32, device=dev)
     gpair = torch.ones(2, dtype=torch.float32, device=dev)
     grad = torch.empty_like(q)
-    ws = torch.empty(lib.sparton_reg_workspace_size(B, Vs), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(lib.sparton_reg_workspace_size(B, Vs), dtype=torch.uint8, device=dev)
     sh, dt = stream.cuda_stream, _lib.DTYPE[c["dtype"]]
 
     def reg_kernels():
@@ -434,7 +434,7 @@ def run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
     """Sparse forms of the head's output for indexing (sparton_b200.sparse), on
     SPLADE-like reps of the workload's shape [B, V_s] (about half the entries
     zero), L2 flushed before every iteration, CUDA events, max over ranks:
-    * csr_kernels: sparton_reps_csr with capacity B*V_s (count, scan, fill);
+    * csr_kernels: sparton_reps_csr with capacity B*V_s (one look-back kernel);
     * csr_api: sparse.reps_to_csr, which reads nnz back to size its output;
     * topk: sparton_reps_topk, k = 256.
     Algorithmic bytes: reps read once plus the output written (CSR: 6 bytes
@@ -452,7 +452,7 @@ def run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
     crow = torch.empty(B + 1, dtype=torch.int64, device=dev)
     cols = torch.empty(B * Vs, dtype=torch.int32, device=dev)
     vals = torch.empty(B * Vs, dtype=c["dtype"], device=dev)
-    ws = torch.empty(max(lib.sparton_sparse_workspace_size(B, Vs), 1), dtype=torch.uint8,
+    ws = torch.zeros(max(lib.sparton_sparse_workspace_size(B, Vs), 1), dtype=torch.uint8,
                      device=dev)
     k = min(256, Vs)
     tv = torch.empty(B, k, dtype=c["dtype"], device=dev)
@@ -500,13 +500,16 @@ def run_transform(args, c, dev, group, world, Vs, flush, stream, barrier, max_ov
     ranks (single GPU: the projection's head is unsharded):
     * kernels_fwd / kernels_bwd: sparton_transform_fwd / _bwd alone (gelu +
       LayerNorm, and its backward with the d_gamma / d_beta / d_bias sums);
-    * projection: SpartonProjection forward + backward (dense GEMMs on cuBLAS,
-      the transform kernels, the head), against
+    * gemm_*: the dense layer's three products on the library's tcgen05 GEMM
+      (y = x Wd^T + bd, dx = dy Wd, dWd = dy^T x; [B*S, D] x [D, D]) against
+      torch's matmuls (cuBLAS), each alone;
+    * projection: SpartonProjection forward + backward (the dense products on
+      the tcgen05 GEMM, the transform kernels, the head), against
     * projection_torch_transform: the same with the transform as torch modules
       (nn.Linear, gelu, nn.LayerNorm: the reference's ProjectionSparton path).
     Algorithmic bytes of the transform kernels: forward reads y and writes h
-    (2·B·S·D·2); backward reads dh and y and writes dy in the row kernel, and
-    reads dh, y, dy in the column kernel (6·B·S·D·2)."""
+    (2·B·S·D·2); backward reads dh and y and writes dy, the column sums
+    coming from the same pass (3·B·S·D·2)."""
     from torch import nn
 
     from sparton_b200 import transform as tr
@@ -565,7 +568,20 @@ def run_transform(args, c, dev, group, world, Vs, flush, stream, barrier, max_ov
     out["kernels_fwd_ms"] = round(timed(lambda: tr.transform_fwd_impl(y, gamma, beta, 1e-12)), 4)
     out["kernels_bwd_ms"] = round(timed(lambda: tr.transform_bwd_impl(dh, y, gamma, mean, rstd)), 4)
     out["kernels_fwd_gbs"] = round(2 * B * S * D * es / (out["kernels_fwd_ms"] * 1e-3) / 1e9, 1)
-    out["kernels_bwd_gbs"] = round(6 * B * S * D * es / (out["kernels_bwd_ms"] * 1e-3) / 1e9, 1)
+    out["kernels_bwd_gbs"] = round(3 * B * S * D * es / (out["kernels_bwd_ms"] * 1e-3) / 1e9, 1)
+    # the dense layer's products alone: ours, then torch (cuBLAS)
+    from sparton_b200.gemm import gemm
+    x2, dy2 = x.view(-1, D), dh.view(-1, D)
+    wd, bd = dense.weight.detach(), dense.bias.detach()
+    flops = 2.0 * B * S * D * D
+    for name, ours, ref in (
+            ("y", lambda: gemm(x2, wd, bias=bd), lambda: torch.nn.functional.linear(x2, wd, bd)),
+            ("dx", lambda: gemm(dy2, wd, b_t=True), lambda: dy2 @ wd),
+            ("dw", lambda: gemm(dy2, x2, a_t=True, b_t=True), lambda: dy2.t() @ x2)):
+        t_ours, t_ref = timed(ours), timed(ref)
+        out[f"gemm_{name}_ms"] = round(t_ours, 4)
+        out[f"gemm_{name}_torch_ms"] = round(t_ref, 4)
+        out[f"gemm_{name}_tflops"] = round(flops / (t_ours * 1e-3) / 1e12, 1)
     if world == 1:
         out["projection_fwd_bwd_ms"] = round(timed(projection), 4)
         out["projection_torch_transform_fwd_bwd_ms"] = round(timed(projection_torch_transform), 4)

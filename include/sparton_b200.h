@@ -207,7 +207,11 @@ int sparton_bwd(const void* grad_reps, const void* reps, const int32_t* idx,
  * Upstream computes them with separate torch reductions; there is no
  * counterpart entry point upstream (these replace those two functions). */
 
-/* Bytes of workspace sparton_reg_fwd needs. */
+/* Bytes of workspace sparton_reg_fwd needs. The workspace must be zero-filled
+ * before its first use (e.g. one cudaMemsetAsync after allocating it); every
+ * call that runs to completion leaves it zero-filled again, so it is reused
+ * as is. One workspace per stream: calls that overlap on the GPU must not
+ * share it. */
 size_t sparton_reg_workspace_size(int64_t B, int64_t V);
 
 /* colsum[v] = sum_b reps[b, v] (fp32, [V], kept for the backward);
@@ -233,7 +237,10 @@ int sparton_reg_bwd(const void* reps, const float* colsum, const float* g_l1,
  * its encode (training/model.py:141-144) returns the dense reps, and
  * training/train.py:205-210 logs the fraction of entries > 0. */
 
-/* Workspace bytes of sparton_reps_csr for reps [B, V]. */
+/* Workspace bytes of sparton_reps_csr for reps [B, V]. Zero-fill it once after
+ * allocating it; it needs no clearing between calls (each call tags the words
+ * it writes). Word 0 is the device status (sparton_read_device_status). One
+ * workspace per stream: calls that overlap on the GPU must not share it. */
 size_t sparton_sparse_workspace_size(int64_t B, int64_t V);
 
 /* CSR of the entries reps[b, v] > threshold, rows in order, columns ascending

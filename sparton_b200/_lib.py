@@ -177,6 +177,24 @@ def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_ZEROED: dict = {}
+
+
+def zeroed_workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
+    """A zero-filled device buffer of at least ``nbytes`` for the entry points
+    whose workspace must be zero when a call starts and is left zero when it
+    ends (sparton_reps_csr, sparton_reg_fwd): one per (device, current stream,
+    tag), cleared once when allocated and reused by every later call on that
+    stream."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream, tag)
+    buf = _ZEROED.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _ZEROED[key] = buf
+    return buf
+
+
 def read_device_status(workspace: torch.Tensor) -> int:
     """Device status word of a forward workspace (0 = no device-side timeout)."""
     code = ctypes.c_uint32(0)

@@ -189,9 +189,9 @@ int launch_reg_bwd(int dtype, const void* reps, const float* colsum, const float
 // Sparse forms of reps (sparse.cu): CSR of the entries above a threshold and
 // the per-row top-k.
 struct SparseWorkspace {
-  unsigned int* header;       // [0] device status (SPARTON_DEV_*), [1] chunk ticket
-  unsigned long long* flags;  // [B][ceil(V / 4096)] the chunks' look-back words
-  size_t bytes;               // header + flags: zeroed before every CSR launch
+  unsigned int* header;       // [0] device status (SPARTON_DEV_*)
+  unsigned long long* flags;  // [ceil(B * V / 8192)] the chunks' look-back words (tagged per call)
+  size_t bytes;               // header + flags
 };
 constexpr int kTopkMax = 4096;
 size_t sparse_workspace_bytes(int64_t B, int64_t V);

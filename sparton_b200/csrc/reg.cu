@@ -9,7 +9,8 @@
 // Here reg_fwd_kernel reads reps once and produces the column sums
 // colsum[v] = sum_b reps[b, v] (kept for the backward) and, per block, the
 // partial sums of |reps| and of colsum^2; the last block to finish (a ticket
-// counter in the workspace, zeroed before the launch) adds the block partials
+// counter in the workspace, zero between calls: the last block clears it) adds
+// the block partials
 // in a fixed order (deterministic) and scales them, giving
 // out = {scale_l1 * sum |reps|, scale_flops * sum_v colsum^2} (1/B and 1/V for
 // the losses; shards' outputs then simply add up). reg_bwd_kernel writes
@@ -30,7 +31,7 @@ namespace sparton {
 namespace {
 
 constexpr int kRegWarps = 8;  // rows are strided over the warps of a block
-constexpr int kRowUnroll = 8;  // row loads of a lane in flight
+constexpr int kRowUnroll = 16;  // row loads of a lane in flight
 
 // kC consecutive columns of a row as fp32 (one 2 * sizeof(T)-byte load for kC = 2).
 template <typename T, int kC>
@@ -168,10 +169,22 @@ __global__ void __launch_bounds__(256)
   const float c1 = g_flops != nullptr ? __ldg(g_flops) * scale_flops : 0.f;
   const long long nvec = n / kPer;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long vi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; vi < nvec;
-       vi += stride) {
+  long long vi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // the column of the thread's first element, and how far it moves per step
+  // (one division each per thread; 32-bit when the offsets fit)
+  int vcol, vstep;
+  if (n <= 0xFFFFFFFFll) {
+    vcol = static_cast<int>(static_cast<unsigned>(vi * kPer) % static_cast<unsigned>(V));
+    vstep = static_cast<int>(static_cast<unsigned>(stride * kPer) % static_cast<unsigned>(V));
+  } else {
+    vcol = static_cast<int>((vi * kPer) % V);
+    vstep = static_cast<int>((stride * kPer) % V);
+  }
+  for (; vi < nvec; vi += stride) {
     const long long g = vi * kPer;
-    int v = static_cast<int>(g % V);
+    int v = vcol;
+    vcol += vstep;
+    if (vcol >= V) vcol -= V;
     if constexpr (kPer == 1) {
       const float x = ldg_f32<T>(reps + g);
       const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
@@ -207,8 +220,6 @@ int launch_fwd_typed(const void* reps, int B, int V, float scale_l1, float scale
                      float* colsum, float* totals, void* workspace, cudaStream_t stream) {
   unsigned int* counter = static_cast<unsigned int*>(workspace);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
-  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned int), stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(reg counter)");
   const bool pairs =
       V % 2 == 0 && reinterpret_cast<uintptr_t>(reps) % (2 * sizeof(T)) == 0;
   if (pairs)
@@ -219,7 +230,7 @@ int launch_fwd_typed(const void* reps, int B, int V, float scale_l1, float scale
     reg_fwd_kernel<T, 1><<<fwd_blocks(V, 1), kRegWarps * 32, 0, stream>>>(
         static_cast<const T*>(reps), B, V, colsum, partials, counter, scale_l1, scale_flops,
         totals);
-  e = cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "reg_fwd_kernel launch");
 }
 
@@ -233,9 +244,9 @@ int launch_bwd_typed(const void* reps, const float* colsum, const float* g_l1,
   const bool vec = reinterpret_cast<uintptr_t>(reps) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(grad) % 16 == 0;
   const long long units = vec ? n / kPer : n;
-  // at most 16 blocks per SM; every thread takes a few vectors
+  // 4 blocks per SM; every thread takes a few vectors
   const long long blocks =
-      std::max(1ll, std::min((units + 255) / 256, 16ll * device_sm_count()));
+      std::max(1ll, std::min((units + 255) / 256, 4ll * device_sm_count()));
   if (vec)
     reg_bwd_kernel<T, kPer><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, n, V,

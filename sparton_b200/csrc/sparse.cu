@@ -6,17 +6,20 @@
 // of entries > 0; an inverted index stores each row's nonzero (vocab id,
 // weight) pairs, or its k heaviest.
 //
-// CSR, one kernel after a memset of its workspace:
-//   csr_kernel  one CTA per chunk of kCsrChunk columns of a row, taken in
-//               row-major order from a ticket counter: counts the entries >
+// CSR, one kernel:
+//   csr_kernel  one CTA per chunk of kCsrChunk elements of the flattened reps:
+//               counts the entries >
 //               threshold, finds the entries of all earlier chunks by a
 //               decoupled look-back over the chunks' published counts and
-//               prefixes, and writes (column, value) in column order; crow[b]
-//               (row starts) and crow[B] (= nnz). Entries at or past
-//               `capacity` are not written (the caller sees nnz in crow[B]).
-// Top-k, a cluster of up to 8 CTAs per row (enough CTAs for two per SM):
-//   radix select on order-preserving unsigned keys (8 bits a pass: 2 passes
-//   for 16-bit types, 4 for fp32), the CTAs' histograms summed through
+//               prefixes, and writes (column, value) in order; crow[b] (row
+//               starts) and crow[B] (= nnz). Entries at or past `capacity` are
+//               not written (the caller sees nnz in crow[B]).
+// Top-k: rows whose keys fit in shared memory (and k <= 512) take
+//   topk_row_kernel, one CTA per row (see there); the others a cluster of up
+//   to 8 CTAs per row (enough CTAs for two per SM):
+//   radix select on order-preserving unsigned keys (12 bits, then 8 bits a
+//   pass, the last the rest: 2 passes for 16-bit types, 4 for fp32), the CTAs'
+//   histograms summed through
 //   distributed shared memory, finds the k-th largest key K and how many of
 //   its equals to take. The first pass reads the row with 16-byte loads; when
 //   few entries share or beat the selected top digit, a second read copies
@@ -28,6 +31,8 @@
 #include <cuda_fp16.h>
 
 #include <cooperative_groups.h>
+#include <atomic>
+#include <type_traits>
 
 #include "dtype.cuh"
 #include "internal.h"
@@ -36,11 +41,13 @@
 namespace sparton {
 namespace {
 
-constexpr int kCsrChunk = 4096;
+constexpr int kCsrChunk = 8192;  // elements of the flattened reps per CTA
 constexpr int kCsrThreads = 256;
 constexpr int kTopkThreads = 512;
 constexpr int kTileU = 8;  // entries per lane per step of a row walk
-constexpr int kTopkCand = 8192;  // candidate list entries per CTA (64 KB of key + id)
+constexpr int kTopkCand = 6144;  // candidate list entries per CTA (48 KB of key + id)
+constexpr int kTopkFirstBits = 12;  // digit width of the first radix pass (4096 bins)
+constexpr int kTopkBins = 1 << kTopkFirstBits;
 
 // Order-preserving unsigned key of an element (larger value -> larger key;
 // NaN above +inf, as torch.topk orders it) and its bit width.
@@ -95,157 +102,202 @@ __device__ __forceinline__ int block_excl_scan(int x, int* tmp, int& total) {
 }
 
 // ------------------------------------------------------------------- CSR
-// Look-back words of the chunks: [status:2][value:62]; status 0 = nothing yet,
-// 1 = the chunk's own count, 2 = the inclusive prefix through the chunk.
-constexpr unsigned long long kLbCount = 1ull << 62;
-constexpr unsigned long long kLbPrefix = 2ull << 62;
-constexpr unsigned long long kLbValue = (1ull << 62) - 1;
+// Look-back words of the chunks: [tag:30][status:2][value:32]. The tag is the
+// call's (the host numbers the calls), so words left by earlier calls never
+// match; status 1 = the chunk's own count, 2 = the inclusive prefix through
+// the chunk.
+constexpr unsigned long long kLbCount = 1ull << 32;
+constexpr unsigned long long kLbPrefix = 2ull << 32;
+constexpr unsigned long long kLbValue = 0xFFFFFFFFull;
+__device__ __forceinline__ unsigned long long lb_word(uint32_t tag, unsigned long long status,
+                                                      unsigned long long value) {
+  return (static_cast<unsigned long long>(tag) << 34) | status | (value & kLbValue);
+}
 
+// The words carry their data (count or prefix) themselves, so relaxed
+// single-copy-atomic 64-bit accesses at GPU scope are enough: no fence orders
+// anything else.
 __device__ __forceinline__ void lb_publish(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long lb_read(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-// One pass (decoupled look-back): a CTA takes the next chunk of kCsrChunk
-// columns in row-major order from a ticket counter (so every chunk before it
-// belongs to a CTA that has already started), loads it into registers, counts
-// the entries above the threshold per (step, warp), publishes its count, and
-// warp 0 walks back over the earlier chunks' words 32 at a time, adding counts
-// until it meets an inclusive prefix; the CTA then publishes its own inclusive
-// prefix and writes its entries at (prefix + earlier steps and warps + earlier
-// u + lower lanes), i.e. columns ascending inside each row. crow[b] is written
-// by the row's first chunk, crow[B] by the last chunk. Entries at or past
-// `capacity` are not written (the caller sees nnz in crow[B]). The waits are
-// on CTAs that are already running and wait on nothing themselves; each is
-// bounded anyway (a timeout records SPARTON_DEV_TIMEOUT_SCAN).
-template <typename T>
+// One pass (decoupled look-back) over the flattened reps [B * V], whose row-
+// major order is the CSR order: CTA c takes the chunk of kCsrChunk elements at
+// c * kCsrChunk. Thread t holds kVecs consecutive vectors of kPer elements
+// (16-byte loads when reps is 16-byte aligned, else kPer = 1) and counts its
+// entries above the threshold; a block prefix over the threads gives each
+// thread's offset inside the chunk, and the chunk publishes its count. Then
+// every thread reads the word of one earlier chunk (kCsrThreads of them per
+// round, nearest first), the block finds the nearest inclusive prefix among
+// them and adds it and the counts after it, and walks further back only if
+// none was there. The CTA publishes its own inclusive prefix; each thread puts
+// its entries (column = flattened index - row * V) in shared memory at its
+// offset, and the CTA copies them to prefix + offset with consecutive threads
+// writing consecutive entries: columns ascending inside each row. crow[b] is written by the
+// thread whose elements include b * V, crow[B] by the last chunk. Entries at
+// or past `capacity` are not written (the caller sees nnz in crow[B]).
+// A chunk waits only for chunks of lower index, which the hardware dispatches
+// first; each wait is bounded anyway (a timeout records
+// SPARTON_DEV_TIMEOUT_SCAN in the workspace header).
+template <typename T, int kPer>
 __global__ void __launch_bounds__(kCsrThreads)
-    csr_kernel(const T* __restrict__ reps, int B, int V, float thr, int nchunks,
+    csr_kernel(const T* __restrict__ reps, int B, int V, float thr, int nchunks, uint32_t tag,
                unsigned int* __restrict__ header, unsigned long long* __restrict__ flags,
                int64_t capacity, int64_t* __restrict__ crow, int32_t* __restrict__ cols,
                T* __restrict__ vals) {
   constexpr int kWarps = kCsrThreads / 32;
-  constexpr int kStepCols = kCsrThreads * kTileU;
-  constexpr int kSteps = kCsrChunk / kStepCols;
-  __shared__ int s_cnt[kSteps * kWarps];
-  __shared__ int s_id;
-  __shared__ long long s_excl;
+  constexpr int kSpan = kCsrChunk / kCsrThreads;  // elements of a thread
+  constexpr int kVecs = kSpan / kPer;
+  __shared__ int tmp[32];
+  __shared__ int s_stop, s_fail;
+  __shared__ long long s_part[kWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const unsigned lt = (1u << lane) - 1u;
-  if (threadIdx.x == 0) s_id = static_cast<int>(atomicAdd(header + 1, 1u));
-  __syncthreads();
-  const int id = s_id;
-  const int b = id / nchunks, ch = id - b * nchunks;
-  const int v0 = ch * kCsrChunk, v1 = min(V, v0 + kCsrChunk);
-  const T* row = reps + static_cast<size_t>(b) * V;
-  T x[kSteps][kTileU];
-  unsigned keep[kSteps][kTileU];
+  if (threadIdx.x == 0) s_fail = 0;
+  const int id = static_cast<int>(blockIdx.x);
+  const long long n = static_cast<long long>(B) * V;
+  const long long e0 = static_cast<long long>(id) * kCsrChunk + static_cast<long long>(threadIdx.x) * kSpan;
+  // the thread's elements e0 .. e0 + nv - 1, kept as loaded (16-byte words)
+  const int nv = static_cast<int>(e0 < n ? (n - e0 < kSpan ? n - e0 : kSpan) : 0);
+  constexpr int kWords = kSpan * static_cast<int>(sizeof(T)) / 4;
+  constexpr int kPerWord = 4 / static_cast<int>(sizeof(T));
+  static_assert(kSpan % kPerWord == 0, "whole 32-bit words per thread");
+  uint32_t w[kWords];
+  // word q of the thread from element loads (the tail of reps, or unaligned reps)
+  auto word_at = [&](int q) -> uint32_t {
+    uint32_t r = 0;
 #pragma unroll
-  for (int st = 0; st < kSteps; ++st)
-#pragma unroll
-    for (int u = 0; u < kTileU; ++u) {
-      const int v = v0 + st * kStepCols + warp * 32 * kTileU + u * 32 + lane;
-      x[st][u] = v < v1 ? row[v] : T{};
+    for (int i = 0; i < kPerWord; ++i) {
+      const int k = q * kPerWord + i;
+      const T t = k < nv ? reps[e0 + k] : T{};
+      uint32_t bits;
+      if constexpr (sizeof(T) == 4)
+        bits = __float_as_uint(to_f32<T>(t));
+      else
+        bits = *reinterpret_cast<const uint16_t*>(&t);
+      r |= bits << (8 * sizeof(T) * i);
     }
+    return r;
+  };
+  if constexpr (kPer > 1) {
+    constexpr int kWordsPerVec = kPer * static_cast<int>(sizeof(T)) / 4;
 #pragma unroll
-  for (int st = 0; st < kSteps; ++st) {
-    int n = 0;
+    for (int u = 0; u < kVecs; ++u) {
+      if ((u + 1) * kPer <= nv) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(reps + e0) + u);
+        w[4 * u] = q.x, w[4 * u + 1] = q.y, w[4 * u + 2] = q.z, w[4 * u + 3] = q.w;
+      } else {
 #pragma unroll
-    for (int u = 0; u < kTileU; ++u) {
-      const int v = v0 + st * kStepCols + warp * 32 * kTileU + u * 32 + lane;
-      keep[st][u] = __ballot_sync(0xFFFFFFFFu, v < v1 && to_f32<T>(x[st][u]) > thr);
-      n += __popc(keep[st][u]);
+        for (int i = 0; i < kWordsPerVec; ++i) w[u * kWordsPerVec + i] = word_at(u * kWordsPerVec + i);
+      }
     }
-    if (lane == 0) s_cnt[st * kWarps + warp] = n;
+  } else {
+#pragma unroll
+    for (int q = 0; q < kWords; ++q) w[q] = word_at(q);
   }
-  __syncthreads();
-  int total = 0;
+  auto elem = [&](int i) -> T { return reinterpret_cast<const T*>(w)[i]; };
+  int cnt = 0;
 #pragma unroll
-  for (int i = 0; i < kSteps * kWarps; ++i) total += s_cnt[i];
-  if (warp == 0) {
-    long long excl = 0;
-    bool ok = true;
-    if (id == 0) {
-      if (lane == 0) lb_publish(flags, kLbPrefix | static_cast<unsigned long long>(total));
-    } else {
-      if (lane == 0) lb_publish(flags + id, kLbCount | static_cast<unsigned long long>(total));
-      const uint64_t t0 = global_timer_ns();
-      for (int pos = id - 1;; pos -= 32) {
-        const int j = pos - lane;  // lane 0 is the nearest earlier chunk
-        unsigned long long f = kLbPrefix;  // before chunk 0: an inclusive prefix of 0
-        if (j >= 0) {
-          f = lb_read(flags + j);
-          while ((f >> 62) == 0) {
-            if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-              ok = false;
-              break;
-            }
-            __nanosleep(64);
-            f = lb_read(flags + j);
-          }
-        }
-        if (!__all_sync(0xFFFFFFFFu, ok)) {
-          ok = false;
+  for (int i = 0; i < kSpan; ++i) cnt += (i < nv && to_f32<T>(elem(i)) > thr) ? 1 : 0;
+  int total;
+  const int before = block_excl_scan(cnt, tmp, total);
+  if (threadIdx.x == 0)
+    lb_publish(flags + id, lb_word(tag, id == 0 ? kLbPrefix : kLbCount,
+                                   static_cast<unsigned long long>(total)));
+  long long excl = 0;
+  const uint64_t t0 = global_timer_ns();
+  const unsigned long long want = static_cast<unsigned long long>(tag) << 34;
+  constexpr unsigned long long kTagMask = ~((1ull << 34) - 1);
+  for (int pos = id - 1; pos >= 0; pos -= kCsrThreads) {
+    const int j = pos - static_cast<int>(threadIdx.x);  // thread 0: the nearest earlier chunk
+    unsigned long long f = 0;
+    if (j >= 0) {
+      f = lb_read(flags + j);
+      while ((f & kTagMask) != want) {
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          s_fail = 1;
           break;
         }
-        const unsigned pre = __ballot_sync(0xFFFFFFFFu, (f >> 62) == 2);
-        const int stop = pre ? __ffs(pre) - 1 : 31;  // the nearest inclusive prefix
-        long long add = lane <= stop ? static_cast<long long>(f & kLbValue) : 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) add += __shfl_xor_sync(0xFFFFFFFFu, add, o);
-        excl += add;
-        if (pre) break;
-      }
-      if (lane == 0) {
-        if (ok)
-          lb_publish(flags + id, kLbPrefix | static_cast<unsigned long long>(excl + total));
-        else
-          atomicCAS(header, 0u, SPARTON_DEV_TIMEOUT_SCAN);
+        __nanosleep(32);
+        f = lb_read(flags + j);
       }
     }
-    if (lane == 0) s_excl = excl;
+    if (threadIdx.x == 0) s_stop = kCsrThreads;
+    __syncthreads();
+    if (j >= 0 && ((f >> 32) & 3ull) == 2) atomicMin(&s_stop, static_cast<int>(threadIdx.x));
+    __syncthreads();
+    const int stop = s_stop;  // the nearest inclusive prefix (kCsrThreads: none)
+    long long add = (j >= 0 && static_cast<int>(threadIdx.x) <= stop)
+                        ? static_cast<long long>(f & kLbValue) : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) add += __shfl_xor_sync(0xFFFFFFFFu, add, o);
+    if (lane == 0) s_part[warp] = add;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) excl += s_part[w];
+    const bool done = stop < kCsrThreads || s_fail;
+    __syncthreads();  // s_part and s_stop are reused
+    if (done) break;
   }
-  __syncthreads();
-  const long long excl = s_excl;
   if (threadIdx.x == 0) {
-    if (ch == 0) crow[b] = excl;
-    if (id == B * nchunks - 1) crow[B] = excl + total;
+    if (s_fail)
+      atomicCAS(header, 0u, SPARTON_DEV_TIMEOUT_SCAN);
+    else if (id > 0)
+      lb_publish(flags + id, lb_word(tag, kLbPrefix, static_cast<unsigned long long>(excl + total)));
+    if (id == nchunks - 1) crow[B] = excl + total;
   }
-  if (capacity <= 0) return;
-  int before = 0;  // entries of the earlier (step, warp) spans
-  for (int i = 0; i < warp; ++i) before += s_cnt[i];
+  // The chunk's entries go to shared memory first (thread order = column
+  // order) and then out to [excl, excl + total) by consecutive threads.
+  extern __shared__ __align__(16) unsigned char csr_smem[];
+  int32_t* s_cols = reinterpret_cast<int32_t*>(csr_smem);             // [kCsrChunk]
+  T* s_vals = reinterpret_cast<T*>(s_cols + kCsrChunk);               // [kCsrChunk]
+  if (nv > 0) {
+    // row and column of the first element; a row starts where the column wraps
+    int row = static_cast<int>(e0 / V);
+    int col = static_cast<int>(e0 - static_cast<long long>(row) * V);
+    int p = before;
+    if (col == 0) crow[row] = excl + p;
 #pragma unroll
-  for (int st = 0; st < kSteps; ++st) {
-    long long at = excl + before;
-#pragma unroll
-    for (int u = 0; u < kTileU; ++u) {
-      if ((keep[st][u] >> lane) & 1u) {
-        const long long i = at + __popc(keep[st][u] & lt);
-        if (i < capacity) {
-          cols[i] = v0 + st * kStepCols + warp * 32 * kTileU + u * 32 + lane;
-          vals[i] = x[st][u];
+    for (int i = 0; i < kSpan; ++i) {
+      if (i < nv) {
+        if (col == V) {
+          col = 0;
+          crow[++row] = excl + p;
         }
+        const T v = elem(i);
+        if (to_f32<T>(v) > thr) {
+          s_cols[p] = col;
+          s_vals[p] = v;
+          ++p;
+        }
+        ++col;
       }
-      at += __popc(keep[st][u]);
     }
-    // the rest of this step, then the next step's warps before this one
-    for (int i = warp; i < kWarps; ++i) before += s_cnt[st * kWarps + i];
-    if (st + 1 < kSteps)
-      for (int i = 0; i < warp; ++i) before += s_cnt[(st + 1) * kWarps + i];
+  }
+  if (capacity <= excl) return;  // (uniform) nothing of this chunk fits
+  __syncthreads();
+  for (int q = threadIdx.x; q < total; q += kCsrThreads) {
+    const long long at = excl + q;
+    if (at < capacity) {
+      cols[at] = s_cols[q];
+      vals[at] = s_vals[q];
+    }
   }
 }
 
 // ------------------------------------------------------------------ top-k
 // A thread-block cluster of P CTAs per row (P = 1 .. 8); CTA c walks the vocab
-// range [c*part, (c+1)*part). Shared memory: hist[256], k_pad (key, id) pairs
+// range [c*part, (c+1)*part). Shared memory: hist[4096], k_pad (key, id) pairs
 // (used in CTA 0), then a candidate list of up to kTopkCand (key, id) pairs.
 //
 // Pass 1 reads the CTA's part with 16-byte loads (kPer elements each; kPer = 1
-// when reps is not 16-byte aligned) and histograms the top 8 key bits; lanes
+// when reps is not 16-byte aligned) and histograms the top 12 key bits (an
+// eighth of an octave for 16-bit types; the later passes take 8 bits, the last
+// the rest); lanes
 // count the key of 0.0 in a register (most entries of a SPLADE row) and add it
 // once. When the cluster's entries at or above the selected digit number at
 // most kTopkCand, a second read of the part (from L2) copies them, in vocab
@@ -288,8 +340,8 @@ __global__ void __launch_bounds__(kTopkThreads)
     topk_kernel(const T* __restrict__ reps, int V, int k, int k_pad, T* __restrict__ out_vals,
                 int32_t* __restrict__ out_idx) {
   extern __shared__ uint32_t smem[];
-  uint32_t* hist = smem;                                          // [256]
-  uint32_t* skey = smem + 256;                                    // [k_pad]
+  uint32_t* hist = smem;                                          // [kTopkBins]
+  uint32_t* skey = smem + kTopkBins;                              // [k_pad]
   int32_t* sid = reinterpret_cast<int32_t*>(skey + k_pad);        // [k_pad]
   uint32_t* ckey = reinterpret_cast<uint32_t*>(sid + k_pad);      // [kTopkCand]
   int32_t* cid = reinterpret_cast<int32_t*>(ckey + kTopkCand);    // [kTopkCand]
@@ -313,34 +365,50 @@ __global__ void __launch_bounds__(kTopkThreads)
     else
       __syncthreads();
   };
-  // Digits in descending order, one per thread: the digit whose bucket holds
-  // the remaining-th largest key of the prefix group (every CTA sums the
-  // cluster's histograms itself and picks the same digit).
-  auto select_digit = [&](uint32_t prefix, uint32_t remaining, int shift) {
+  // The digit whose bucket holds the remaining-th largest key of the prefix
+  // group, over nbins digits of width `shift`..: thread t owns the `per`
+  // digits nbins-1 - t*per - [0, per) (descending); every CTA sums the
+  // cluster's histograms itself and picks the same digit.
+  auto select_digit = [&](uint32_t prefix, uint32_t remaining, int shift, int nbins) {
+    const int per = nbins > kTopkThreads ? nbins / kTopkThreads : 1;
     const int t = static_cast<int>(threadIdx.x);
-    uint32_t own = 0, before = 0;
-    if (t < 256) {
-      if (P == 1) {
-        own = hist[255 - t];
-      } else {
-        for (int r = 0; r < P; ++r) {
-          const uint32_t x = *cluster.map_shared_rank(hist + (255 - t), r);
-          own += x;
-          before += r < c ? x : 0u;
+    uint32_t cnt[kTopkBins / kTopkThreads], bef[kTopkBins / kTopkThreads];
+    uint32_t own = 0;
+#pragma unroll
+    for (int q = 0; q < kTopkBins / kTopkThreads; ++q) {
+      const int dgt = nbins - 1 - (t * per + q);
+      cnt[q] = bef[q] = 0;
+      if (q < per && dgt >= 0) {
+        if (P == 1) {
+          cnt[q] = hist[dgt];
+        } else {
+          for (int r = 0; r < P; ++r) {
+            const uint32_t x = *cluster.map_shared_rank(hist + dgt, r);
+            cnt[q] += x;
+            bef[q] += r < c ? x : 0u;
+          }
         }
+        own += cnt[q];
       }
     }
     int total;
-    const uint32_t above = static_cast<uint32_t>(block_excl_scan(static_cast<int>(own), tmp, total));
-    if (t < 256 && above < remaining && above + own >= remaining) {
-      s_prefix = prefix | (static_cast<uint32_t>(255 - t) << shift);
-      s_remaining = remaining - above;
-      s_eq_before = before;  // after the last pass: equals of K in the CTAs before this one
-      s_cge = above + own;   // entries of the group at or above the digit
+    uint32_t above = static_cast<uint32_t>(block_excl_scan(static_cast<int>(own), tmp, total));
+    if (above < remaining && above + own >= remaining) {
+#pragma unroll
+      for (int q = 0; q < kTopkBins / kTopkThreads; ++q) {
+        if (q < per && above + cnt[q] >= remaining) {
+          s_prefix = prefix | (static_cast<uint32_t>(nbins - 1 - (t * per + q)) << shift);
+          s_remaining = remaining - above;
+          s_eq_before = bef[q];       // after the last pass: equals of K in the CTAs before this one
+          s_cge = above + cnt[q];     // entries of the group at or above the digit
+          break;
+        }
+        above += cnt[q];
+      }
     }
   };
 
-  // ---- pass 1: the top 8 bits, 16-byte loads
+  // ---- pass 1: the top kTopkFirstBits bits, 16-byte loads
   const size_t g0 = static_cast<size_t>(b) * V + v_lo;
   const size_t a0 = g0 / kPer * kPer;
   const int lo = static_cast<int>(g0 - a0), hi = lo + (v_hi - v_lo);  // element offsets from a0
@@ -348,8 +416,8 @@ __global__ void __launch_bounds__(kTopkThreads)
   const T* abase = reps + a0;
   constexpr int kVU = kPer == 1 ? 8 : 2;  // loads per lane per step
   constexpr int kVStep = kTopkThreads * kVU;
-  const int shift0 = kBits - 8;
-  for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
+  const int shift0 = kBits - kTopkFirstBits;
+  for (int i = threadIdx.x; i < kTopkBins; i += kTopkThreads) hist[i] = 0;
   if (threadIdx.x == 0) s_gt = 0;
   __syncthreads();
   {
@@ -364,14 +432,25 @@ __global__ void __launch_bounds__(kTopkThreads)
 #pragma unroll
       for (int u = 0; u < kVU; ++u) {
         const int vi = base + u * 32 + lane;
+        const int off0 = vi * kPer;
+        if (vi < nvec && off0 >= lo && off0 + kPer <= hi) {  // a whole vector of the part
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) {
-          const int off = vi * kPer + e;
-          if (vi < nvec && off >= lo && off < hi) {
+          for (int e = 0; e < kPer; ++e) {
             if (key[u][e] == kZeroKey)
               ++zc;
             else
               atomicAdd(&hist[key[u][e] >> shift0], 1u);
+          }
+        } else if (vi < nvec) {
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) {
+            const int off = off0 + e;
+            if (off >= lo && off < hi) {
+              if (key[u][e] == kZeroKey)
+                ++zc;
+              else
+                atomicAdd(&hist[key[u][e] >> shift0], 1u);
+            }
           }
         }
       }
@@ -381,10 +460,10 @@ __global__ void __launch_bounds__(kTopkThreads)
     if (lane == 0 && zc) atomicAdd(&hist[kZeroKey >> shift0], zc);
   }
   csync();  // every CTA's histogram is complete
-  select_digit(0u, static_cast<uint32_t>(k), shift0);
+  select_digit(0u, static_cast<uint32_t>(k), shift0, kTopkBins);
   csync();  // no CTA reads another's histogram past this point
   uint32_t prefix = s_prefix, remaining = s_remaining;
-  uint32_t prefix_mask = 0xFFu << shift0;
+  uint32_t prefix_mask = (kTopkBins - 1u) << shift0;
   const bool use_list = s_cge <= static_cast<uint32_t>(kTopkCand);
 
   // ---- the candidate list: entries whose top digit is >= the selected one
@@ -444,13 +523,17 @@ __global__ void __launch_bounds__(kTopkThreads)
   constexpr int kStep = kTopkThreads * kTileU;
 
   // ---- the remaining radix passes
-  for (int shift = kBits - 16; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
+  for (int shift = shift0; shift > 0;) {
+    const int width = shift < 8 ? shift : 8;
+    shift -= width;
+    const uint32_t dmask = (1u << width) - 1u;
+    constexpr uint32_t kNoDigit = 0xFFFFu;
+    for (int i = threadIdx.x; i < (1 << width); i += kTopkThreads) hist[i] = 0;
     __syncthreads();
     // when the key of 0.0 is still in the prefix group its digit is the
     // common one, otherwise lane 0's
     const bool zero_in_group = (kZeroKey & prefix_mask) == prefix;
-    const uint32_t zero_digit = (kZeroKey >> shift) & 0xFFu;
+    const uint32_t zero_digit = (kZeroKey >> shift) & dmask;
     for (int base = warp * 32 * kTileU; base < n_src; base += kStep) {
       uint32_t key[kTileU];
 #pragma unroll
@@ -462,24 +545,24 @@ __global__ void __launch_bounds__(kTopkThreads)
       for (int u = 0; u < kTileU; ++u) {
         const int i = base + u * 32 + lane;
         const uint32_t d =
-            (i < n_src && (key[u] & prefix_mask) == prefix) ? (key[u] >> shift) & 0xFFu : 256u;
+            (i < n_src && (key[u] & prefix_mask) == prefix) ? (key[u] >> shift) & dmask : kNoDigit;
         // The lanes holding the common digit add once (one ballot); the rest
         // add one each.
         const uint32_t dc = zero_in_group ? zero_digit : __shfl_sync(0xFFFFFFFFu, d, 0);
         const unsigned same = __ballot_sync(0xFFFFFFFFu, d == dc);
         if (d == dc) {
-          if (d < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[d], __popc(same));
-        } else if (d < 256u) {
+          if (d != kNoDigit && lane == __ffs(same) - 1) atomicAdd(&hist[d], __popc(same));
+        } else if (d != kNoDigit) {
           atomicAdd(&hist[d], 1u);
         }
       }
     }
     csync();
-    select_digit(prefix, remaining, shift);
+    select_digit(prefix, remaining, shift, 1 << width);
     csync();
     prefix = s_prefix;
     remaining = s_remaining;
-    prefix_mask |= 0xFFu << shift;
+    prefix_mask |= dmask << shift;
   }
   // K = prefix (all bits); take every key > K and the first `remaining`
   // equals in vocab order (rank = equals in earlier CTAs, then in earlier
@@ -564,23 +647,270 @@ __global__ void __launch_bounds__(kTopkThreads)
   }
 }
 
+// ------------------------------------------------ top-k, rows in shared memory
+// One CTA of kRowThreads per row whose keys fit in shared memory (V * key size
+// <= kRowStageBytes) and k <= kRowMaxK:
+//   1. the row is read once with 16-byte loads; its order-preserving keys go
+//      to shared memory (vector i of the aligned-down row at key offset
+//      i * kPer) and the top kTopkFirstBits of each key into a histogram
+//      (the key of 0.0 is counted in registers and added once per warp);
+//   2. the digit holding the k-th largest key is selected; while more than
+//      kRowList entries lie at or above it and key bits remain, one more
+//      histogram pass over the staged keys of the selected group narrows it;
+//   3. the entries at or above the threshold (at most kRowList) are copied
+//      into a list of (key << 32 | ~vocab id) words, each warp reserving its
+//      slots with one shared atomic; when ties of the exact k-th key
+//      overflow the list instead, the list gets the entries above it and the
+//      first equals in vocab order (block prefix counts per step);
+//   4. each list entry's rank is the number of entries before it in (key
+//      descending, vocab id ascending) order, a strict total order, so the
+//      entries of rank < k go straight to their output slots.
+constexpr int kRowThreads = 1024;
+constexpr int kRowList = 1024;
+constexpr int kRowMaxK = 512;
+constexpr size_t kRowStageBytes = 128 * 1024;
+
+template <typename T>
+using RowKey = typename std::conditional<sizeof(T) == 2, uint16_t, uint32_t>::type;
+
+template <typename T, int kPer>
+__global__ void __launch_bounds__(kRowThreads)
+    topk_row_kernel(const T* __restrict__ reps, int V, int k, T* __restrict__ out_vals,
+                    int32_t* __restrict__ out_idx) {
+  using KeyT = RowKey<T>;
+  extern __shared__ __align__(16) unsigned char smem_row[];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem_row);                          // [kTopkBins]
+  unsigned long long* list = reinterpret_cast<unsigned long long*>(hist + kTopkBins);  // [kRowList]
+  KeyT* skey = reinterpret_cast<KeyT*>(list + kRowList);                          // [nvec * kPer]
+  __shared__ int tmp[32];
+  __shared__ uint32_t s_prefix, s_remaining, s_cge, s_n;
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  constexpr int kBits = Key<T>::kBits;
+  constexpr uint32_t kZeroKey = 1u << (kBits - 1);
+  constexpr int kU = 4;  // vectors of a thread in flight
+  const int shift0 = kBits - kTopkFirstBits;
+  const T* row = reps + static_cast<size_t>(b) * V;
+  const size_t g0 = static_cast<size_t>(b) * V;
+  const size_t a0 = g0 / kPer * kPer;
+  const int lo = static_cast<int>(g0 - a0), hi = lo + V;  // key offsets of the row's entries
+  const int nvec = (hi + kPer - 1) / kPer;
+  for (int i = threadIdx.x; i < kTopkBins; i += kRowThreads) hist[i] = 0;
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+
+  // ---- 1. stage the keys, histogram of the top digit
+  {
+    uint32_t zc = 0;
+    for (int base = threadIdx.x; base < nvec; base += kU * kRowThreads) {
+      uint32_t key[kU][kPer];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int vi = base + u * kRowThreads;
+        if (vi < nvec) load_keys<T, kPer>(reps + a0, vi, key[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int vi = base + u * kRowThreads;
+        if (vi >= nvec) continue;
+        if constexpr (kPer == 1) {
+          skey[vi] = static_cast<KeyT>(key[u][0]);
+        } else if constexpr (sizeof(KeyT) == 2) {
+          uint4 w;
+          w.x = key[u][0] | (key[u][1] << 16);
+          w.y = key[u][2] | (key[u][3] << 16);
+          w.z = key[u][4] | (key[u][5] << 16);
+          w.w = key[u][6] | (key[u][7] << 16);
+          *reinterpret_cast<uint4*>(skey + vi * kPer) = w;
+        } else {
+          *reinterpret_cast<uint4*>(skey + vi * kPer) =
+              make_uint4(key[u][0], key[u][1], key[u][2], key[u][3]);
+        }
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const int off = vi * kPer + e;
+          if (off >= lo && off < hi) {
+            if (key[u][e] == kZeroKey)
+              ++zc;
+            else
+              atomicAdd(&hist[key[u][e] >> shift0], 1u);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) zc += __shfl_xor_sync(0xFFFFFFFFu, zc, o);
+    if (lane == 0 && zc) atomicAdd(&hist[kZeroKey >> shift0], zc);
+  }
+  __syncthreads();
+
+  // The digit (of nbins) holding the remaining-th largest key of the prefix
+  // group: thread t owns digits nbins-1 - t*per - [0, per), descending.
+  auto select_digit = [&](uint32_t prefix, uint32_t remaining, int shift, int nbins) {
+    const int per = nbins > kRowThreads ? nbins / kRowThreads : 1;
+    const int t = static_cast<int>(threadIdx.x);
+    constexpr int kPerMax = kTopkBins / kRowThreads;
+    uint32_t cnt[kPerMax];
+    uint32_t own = 0;
+#pragma unroll
+    for (int q = 0; q < kPerMax; ++q) {
+      const int dgt = nbins - 1 - (t * per + q);
+      cnt[q] = (q < per && dgt >= 0) ? hist[dgt] : 0u;
+      own += cnt[q];
+    }
+    int total;
+    uint32_t above = static_cast<uint32_t>(block_excl_scan(static_cast<int>(own), tmp, total));
+    if (above < remaining && above + own >= remaining) {
+#pragma unroll
+      for (int q = 0; q < kPerMax; ++q) {
+        if (q < per && above + cnt[q] >= remaining) {
+          s_prefix = prefix | (static_cast<uint32_t>(nbins - 1 - (t * per + q)) << shift);
+          s_remaining = remaining - above;
+          s_cge = above + cnt[q];
+          break;
+        }
+        above += cnt[q];
+      }
+    }
+  };
+
+  // ---- 2. select, narrowing while the candidates overflow the list
+  select_digit(0u, static_cast<uint32_t>(k), shift0, kTopkBins);
+  __syncthreads();
+  uint32_t prefix = s_prefix, remaining = s_remaining;
+  uint32_t cge = s_cge;  // entries with key >= prefix
+  uint32_t pmask = (kTopkBins - 1u) << shift0;
+  int shift = shift0;
+  while (cge > static_cast<uint32_t>(kRowList) && shift > 0) {
+    const int width = shift < 8 ? shift : 8;
+    shift -= width;
+    const uint32_t dmask = (1u << width) - 1u;
+    __syncthreads();  // the previous select's reads of hist are done
+    for (int i = threadIdx.x; i < (1 << width); i += kRowThreads) hist[i] = 0;
+    __syncthreads();
+    uint32_t zc = 0;
+    const bool zero_in_group = (kZeroKey & pmask) == prefix;
+    for (int off = lo + threadIdx.x; off < hi; off += kRowThreads) {
+      const uint32_t key = skey[off];
+      if ((key & pmask) == prefix) {
+        if (zero_in_group && key == kZeroKey)
+          ++zc;
+        else
+          atomicAdd(&hist[(key >> shift) & dmask], 1u);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) zc += __shfl_xor_sync(0xFFFFFFFFu, zc, o);
+    if (lane == 0 && zc) atomicAdd(&hist[(kZeroKey >> shift) & dmask], zc);
+    __syncthreads();
+    const uint32_t above_group = static_cast<uint32_t>(k) - remaining;
+    select_digit(prefix, remaining, shift, 1 << width);
+    __syncthreads();
+    prefix = s_prefix;
+    remaining = s_remaining;
+    cge = above_group + s_cge;
+    pmask |= dmask << shift;
+  }
+
+  // ---- 3. the list
+  if (cge <= static_cast<uint32_t>(kRowList)) {
+    // every entry with key >= prefix (lower bits of prefix are 0)
+    for (int off0 = lo + 32 * (threadIdx.x >> 5); off0 < hi; off0 += kRowThreads) {
+      const int off = off0 + lane;
+      const uint32_t key = off < hi ? static_cast<uint32_t>(skey[off]) : 0u;
+      const bool take = off < hi && key >= prefix;
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, take);
+      if (m == 0u) continue;
+      uint32_t at = 0;
+      if (lane == 0) at = atomicAdd(&s_n, static_cast<uint32_t>(__popc(m)));
+      at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(m & ((1u << lane) - 1u));
+      if (take)
+        list[at] = (static_cast<unsigned long long>(key) << 32) |
+                   (0xFFFFFFFFu - static_cast<uint32_t>(off - lo));
+    }
+  } else {
+    // K = prefix exactly: the entries above K, then the first `remaining`
+    // equals in vocab order (thread t of a step takes 32 consecutive entries
+    // of a warp-strided span: rank = equals in earlier steps and threads)
+    const uint32_t K = prefix;
+    const uint32_t n_gt = static_cast<uint32_t>(k) - remaining;
+    int eq_seen = 0;
+    for (int off0 = lo; off0 < hi; off0 += kRowThreads * 32) {
+      const int mine = off0 + 32 * static_cast<int>(threadIdx.x);
+      int c_eq = 0;
+      for (int j = 0; j < 32; ++j) {
+        const int off = mine + j;
+        if (off < hi) {
+          const uint32_t key = skey[off];
+          if (key > K) {
+            const uint32_t at = atomicAdd(&s_n, 1u);
+            list[at] = (static_cast<unsigned long long>(key) << 32) |
+                       (0xFFFFFFFFu - static_cast<uint32_t>(off - lo));
+          }
+          c_eq += key == K;
+        }
+      }
+      int total;
+      int r = eq_seen + block_excl_scan(c_eq, tmp, total);
+      for (int j = 0; j < 32 && r < static_cast<int>(remaining); ++j) {
+        const int off = mine + j;
+        if (off < hi && skey[off] == K) {
+          list[n_gt + r] = (static_cast<unsigned long long>(K) << 32) |
+                           (0xFFFFFFFFu - static_cast<uint32_t>(off - lo));
+          ++r;
+        }
+      }
+      eq_seen += total;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_n = static_cast<uint32_t>(k);
+  }
+  __syncthreads();
+
+  // ---- 4. rank = entries before this one; rank < k goes to the output
+  const int m = static_cast<int>(s_n);
+  for (int t = threadIdx.x; t < m; t += kRowThreads) {
+    const unsigned long long c = list[t];
+    int rank = 0;
+    int j = 0;
+    for (; j + 4 <= m; j += 4)
+      rank += (list[j] > c) + (list[j + 1] > c) + (list[j + 2] > c) + (list[j + 3] > c);
+    for (; j < m; ++j) rank += list[j] > c;
+    if (rank < k) {
+      const int v = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(c));
+      out_idx[static_cast<size_t>(b) * k + rank] = v;
+      out_vals[static_cast<size_t>(b) * k + rank] = row[v];
+    }
+  }
+}
+
 template <typename T>
 int launch_csr_typed(const void* reps, int B, int V, float thr, int64_t* crow, int32_t* cols,
                      void* vals, int64_t capacity, const SparseWorkspace& ws,
                      cudaStream_t stream) {
-  const int nchunks = (V + kCsrChunk - 1) / kCsrChunk;
-  if (B == 0 || nchunks == 0) {  // every row empty
+  if (B == 0 || V == 0) {  // every row empty
     const cudaError_t e =
         cudaMemsetAsync(crow, 0, (static_cast<size_t>(B) + 1) * sizeof(int64_t), stream);
     return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "cudaMemsetAsync(crow)");
   }
-  // status, ticket and look-back words start at zero
-  cudaError_t e = cudaMemsetAsync(ws.header, 0, ws.bytes, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(csr workspace)");
-  const int n = B * nchunks;
-  csr_kernel<T><<<n, kCsrThreads, 0, stream>>>(static_cast<const T*>(reps), B, V, thr, nchunks,
-                                                ws.header, ws.flags, capacity, crow, cols,
-                                                static_cast<T*>(vals));
+  // this call's tag for the look-back words (30 bits, never 0)
+  static std::atomic<uint32_t> calls{0};
+  const uint32_t tag = (calls.fetch_add(1, std::memory_order_relaxed) % 0x3FFFFFFFu) + 1u;
+  const int n = static_cast<int>((static_cast<long long>(B) * V + kCsrChunk - 1) / kCsrChunk);
+  const size_t smem = static_cast<size_t>(kCsrChunk) * (sizeof(int32_t) + sizeof(T));
+  const bool vec = reinterpret_cast<uintptr_t>(reps) % 16 == 0;
+  cudaError_t e = cudaFuncSetAttribute(vec ? csr_kernel<T, 16 / sizeof(T)> : csr_kernel<T, 1>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_fail(e, "csr_kernel smem");
+  if (vec)
+    csr_kernel<T, 16 / sizeof(T)><<<n, kCsrThreads, smem, stream>>>(
+        static_cast<const T*>(reps), B, V, thr, n, tag, ws.header, ws.flags, capacity, crow, cols,
+        static_cast<T*>(vals));
+  else
+    csr_kernel<T, 1><<<n, kCsrThreads, smem, stream>>>(static_cast<const T*>(reps), B, V, thr, n, tag,
+                                                     ws.header, ws.flags, capacity, crow, cols,
+                                                     static_cast<T*>(vals));
   e = cudaGetLastError();
   return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "csr_kernel launch");
 }
@@ -591,7 +921,7 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
   if (B == 0 || k == 0) return SPARTON_OK;
   int k_pad = 1;
   while (k_pad < k) k_pad <<= 1;
-  const size_t smem = (256 + 2 * static_cast<size_t>(k_pad) + 2 * static_cast<size_t>(kTopkCand)) *
+  const size_t smem = (kTopkBins + 2 * static_cast<size_t>(k_pad) + 2 * static_cast<size_t>(kTopkCand)) *
                       sizeof(uint32_t);
   // Enough CTAs for two per SM, each walking at least 16384 entries of its
   // row (shorter spans lose more to the cluster barriers than they gain).
@@ -611,7 +941,22 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
   cfg.numAttrs = 1;
   // 16-byte loads in the first passes when the rows' storage is 16-byte aligned
   const bool vec = reinterpret_cast<uintptr_t>(reps) % 16 == 0;
-  auto kernel = vec ? topk_kernel<T, 16 / sizeof(T)> : topk_kernel<T, 1>;
+  constexpr int kPerVec = 16 / sizeof(T);
+  const size_t row_keys = (static_cast<size_t>(V) + 2 * kPerVec) * sizeof(RowKey<T>);
+  if (k <= kRowMaxK && row_keys <= kRowStageBytes) {
+    // the row's keys fit in shared memory: one CTA per row
+    const size_t rsmem = kTopkBins * sizeof(uint32_t) + kRowList * sizeof(unsigned long long) +
+                         (row_keys + 15) / 16 * 16;
+    auto rkernel = vec ? topk_row_kernel<T, kPerVec> : topk_row_kernel<T, 1>;
+    cudaError_t e = cudaFuncSetAttribute(rkernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(rsmem));
+    if (e != cudaSuccess) return cuda_fail(e, "topk_row_kernel smem");
+    rkernel<<<B, kRowThreads, rsmem, stream>>>(static_cast<const T*>(reps), V, k,
+                                               static_cast<T*>(vals), idx);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? SPARTON_OK : cuda_fail(e, "topk_row_kernel launch");
+  }
+  auto kernel = vec ? topk_kernel<T, kPerVec> : topk_kernel<T, 1>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return cuda_fail(e, "topk_kernel smem");
@@ -631,18 +976,16 @@ int launch_topk_typed(const void* reps, int B, int V, int k, void* vals, int32_t
 }  // namespace
 
 size_t sparse_workspace_bytes(int64_t B, int64_t V) {
-  const int64_t nchunks = (V + kCsrChunk - 1) / kCsrChunk;
-  const int64_t n = (B > 0 ? B : 1) * (nchunks > 0 ? nchunks : 1);
-  return 256 + align256(static_cast<size_t>(n) * sizeof(unsigned long long));
+  const int64_t n = ((B > 0 ? B : 0) * (V > 0 ? V : 0) + kCsrChunk - 1) / kCsrChunk;
+  return 256 + align256(static_cast<size_t>(n > 0 ? n : 1) * sizeof(unsigned long long));
 }
 
 SparseWorkspace sparse_workspace_carve(void* base, int64_t B, int64_t V) {
-  const int64_t nchunks = (V + kCsrChunk - 1) / kCsrChunk;
+  const int64_t n = ((B > 0 ? B : 0) * (V > 0 ? V : 0) + kCsrChunk - 1) / kCsrChunk;
   SparseWorkspace ws;
   ws.header = static_cast<unsigned int*>(base);
   ws.flags = reinterpret_cast<unsigned long long*>(static_cast<char*>(base) + 256);
-  ws.bytes = 256 + static_cast<size_t>(B > 0 ? B : 0) * static_cast<size_t>(nchunks) *
-                       sizeof(unsigned long long);
+  ws.bytes = 256 + static_cast<size_t>(n) * sizeof(unsigned long long);
   return ws;
 }
 

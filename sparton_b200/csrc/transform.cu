@@ -262,24 +262,32 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 // l + 32, ... One erff and one expf per element: the first pass keeps (dh,
 // xh, gelu'(y)) of each element in registers, the second writes dy and adds
 // dh * xh, dh and the rounded dy into the warp's column sums in shared memory
-// (each lane its own columns: no conflicts, no atomics). The CTA then adds
-// its warps' sums in warp order into partials[c][k][col] (k = gamma, beta,
-// bias) when partials is not NULL. The grid depends on rows only, so the
-// column sums are deterministic.
+// (each lane its own columns: no atomics). Shared arrays indexed by a lane's
+// column are stored lane-minor, element (j, i) of lane l at (j * 8 + i) * 32
+// + l, so a warp's accesses fall in 32 distinct banks. The CTA then adds its
+// warps' sums in warp order into partials[c][k][col] (k = gamma, beta, bias)
+// when partials is not NULL. The grid depends on rows only, so the column
+// sums are deterministic.
 template <typename T, int kNv>
 __global__ void __launch_bounds__(kRowWarps * 32, 2)
     transform_bwd_fused_kernel(const T* __restrict__ dh, const T* __restrict__ y,
                                const T* __restrict__ gamma, const float* __restrict__ mean,
                                const float* __restrict__ rstd, int rows, int D,
                                T* __restrict__ dy, float* __restrict__ partials) {
+  constexpr int kSlots = kNv * 8 * 32;  // lane-minor slots of one [D] array
   extern __shared__ float sh[];
-  float* sgamma = sh;                                     // [D]
+  float* sgamma = sh;                   // [kSlots]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* acc = sh + D + static_cast<size_t>(warp) * 3 * D;  // this warp's [3][D]
+  float* acc = sh + kSlots + static_cast<size_t>(warp) * 3 * kSlots;  // this warp's [3][kSlots]
   const bool want = partials != nullptr;
-  for (int i = threadIdx.x; i < D; i += kRowWarps * 32) sgamma[i] = to_f32<T>(gamma[i]);
+  auto slot = [](int d) {  // column d -> its lane-minor slot
+    const int j = d >> 8, l = (d >> 3) & 31, i = d & 7;
+    return (j * 8 + i) * 32 + l;
+  };
+  for (int d = threadIdx.x; d < kNv * 256; d += kRowWarps * 32)
+    sgamma[slot(d)] = d < D ? to_f32<T>(gamma[d]) : 0.f;
   if (want)
-    for (int i = lane; i < 3 * D; i += 32) acc[i] = 0.f;
+    for (int i = lane; i < 3 * kSlots; i += 32) acc[i] = 0.f;
   __syncthreads();
   const long long r_lo = static_cast<long long>(blockIdx.x) * rows / gridDim.x;
   const long long r_hi = static_cast<long long>(blockIdx.x + 1) * rows / gridDim.x;
@@ -303,7 +311,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 2)
           const float g = to_f32<T>(from_f32<T>(0.5f * yv[i] * (1.f + e)));
           gp[j][i] = 0.5f * (1.f + e) + yv[i] * 0.39894228040143268f * expf(-0.5f * yv[i] * yv[i]);
           xh[j][i] = (g - mu) * rs;
-          const float dxh = gv[j][i] * sgamma[d + i];
+          const float dxh = gv[j][i] * sgamma[(j * 8 + i) * 32 + lane];
           a += dxh;
           b += dxh * xh[j][i];
         }
@@ -318,17 +326,15 @@ __global__ void __launch_bounds__(kRowWarps * 32, 2)
         float out[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          out[i] = rs * (gv[j][i] * sgamma[d + i] - a - xh[j][i] * b) * gp[j][i];
+          out[i] = rs * (gv[j][i] * sgamma[(j * 8 + i) * 32 + lane] - a - xh[j][i] * b) * gp[j][i];
         store8<T>(dy + o + d, out);
         if (want) {
-          float* pg = acc + d;
-          float* pb = acc + D + d;
-          float* pd = acc + 2 * D + d;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            pg[i] += gv[j][i] * xh[j][i];
-            pb[i] += gv[j][i];
-            pd[i] += to_f32<T>(from_f32<T>(out[i]));
+            const int q = (j * 8 + i) * 32 + lane;
+            acc[q] += gv[j][i] * xh[j][i];
+            acc[kSlots + q] += gv[j][i];
+            acc[2 * kSlots + q] += to_f32<T>(from_f32<T>(out[i]));
           }
         }
       }
@@ -336,11 +342,13 @@ __global__ void __launch_bounds__(kRowWarps * 32, 2)
   }
   if (!want) return;
   __syncthreads();
-  const float* all = sh + D;
+  const float* all = sh + kSlots;
   for (int c = threadIdx.x; c < 3 * D; c += kRowWarps * 32) {
+    const int k = c / D, d = c - k * D;
+    const int q = k * kSlots + slot(d);
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kRowWarps; ++w) t += all[static_cast<size_t>(w) * 3 * D + c];
+    for (int w = 0; w < kRowWarps; ++w) t += all[static_cast<size_t>(w) * 3 * kSlots + q];
     partials[static_cast<size_t>(blockIdx.x) * 3 * D + c] = t;
   }
 }
@@ -473,7 +481,10 @@ int fwd_typed(const void* y, const void* gamma, const void* beta, float eps, int
 // column sums' order depends on the shape only), at least 8 rows each.
 constexpr int kFusedCtas = 2 * 148;
 int fused_grid(int rows) { return std::max(1, std::min(kFusedCtas, (rows + 7) / 8)); }
-size_t fused_smem(int D) { return (static_cast<size_t>(D) + kRowWarps * 3 * D) * sizeof(float); }
+size_t fused_smem(int D) {
+  const size_t slots = static_cast<size_t>((D + 255) / 256) * 256;  // kNv * 8 * 32
+  return (slots + kRowWarps * 3 * slots) * sizeof(float);
+}
 
 template <typename T, int kNv>
 int bwd_fused(const void* dh, const void* y, const void* gamma, const float* mean,

@@ -51,7 +51,7 @@ def reg_forward_impl(reps: torch.Tensor, scale_l1: float,
     dev = reps.device
     colsum = torch.empty(V, dtype=torch.float32, device=dev)
     out = torch.empty(2, dtype=torch.float32, device=dev)
-    ws = torch.empty(max(lib.sparton_reg_workspace_size(B, V), 1), dtype=torch.uint8, device=dev)
+    ws = _lib.zeroed_workspace(dev, lib.sparton_reg_workspace_size(B, V), "reg")
     with torch.cuda.device(dev):
         st = lib.sparton_reg_fwd(_lib.ptr(reps), _lib.DTYPE[reps.dtype], B, V, scale_l1,
                                  scale_flops, _lib.ptr(colsum), _lib.ptr(out), _lib.ptr(ws),

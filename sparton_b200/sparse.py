@@ -52,8 +52,7 @@ def csr_arrays(reps: torch.Tensor, threshold: float = 0.0
     dev = reps.device
     dt = _lib.DTYPE[reps.dtype]
     crow = torch.empty(B + 1, dtype=torch.int64, device=dev)
-    ws = torch.empty(max(lib.sparton_sparse_workspace_size(B, V), 1), dtype=torch.uint8,
-                     device=dev)
+    ws = _lib.zeroed_workspace(dev, lib.sparton_sparse_workspace_size(B, V), "csr")
     sh = _lib.stream_handle(dev)
     with torch.cuda.device(dev):
         _lib.check(lib.sparton_reps_csr(_lib.ptr(reps), dt, B, V, float(threshold),
@@ -99,8 +98,7 @@ def nonzero_ratio(reps: torch.Tensor) -> torch.Tensor:
     B, V = reps.shape
     dev = reps.device
     crow = torch.empty(B + 1, dtype=torch.int64, device=dev)
-    ws = torch.empty(max(lib.sparton_sparse_workspace_size(B, V), 1), dtype=torch.uint8,
-                     device=dev)
+    ws = _lib.zeroed_workspace(dev, lib.sparton_sparse_workspace_size(B, V), "csr")
     with torch.cuda.device(dev):
         st = lib.sparton_reps_csr(_lib.ptr(reps), _lib.DTYPE[reps.dtype], B, V, 0.0,
                                   _lib.ptr(crow), None, None, 0, _lib.ptr(ws), ws.numel(),

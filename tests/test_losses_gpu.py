@@ -66,7 +66,7 @@ def test_reg_capi_direct():
     x = _reps(16, 999, torch.bfloat16, seed=4).cuda()
     colsum = torch.empty(999, dtype=torch.float32, device="cuda")
     out = torch.empty(2, dtype=torch.float32, device="cuda")
-    ws = torch.empty(lib.sparton_reg_workspace_size(16, 999), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(lib.sparton_reg_workspace_size(16, 999), dtype=torch.uint8, device="cuda")
     sh = torch.cuda.current_stream().cuda_stream
     assert lib.sparton_reg_fwd(x.data_ptr(), 2, 16, 999, 0.5, 0.25, colsum.data_ptr(),
                                out.data_ptr(), ws.data_ptr(), ws.numel(), sh) == 0

@@ -134,7 +134,7 @@ def test_csr_tensor_and_capi_capacity():
     cap = 100
     cols = torch.full((cap + 8,), -1, dtype=torch.int32, device="cuda")
     vals = torch.zeros(cap + 8, dtype=torch.float16, device="cuda")
-    ws = torch.empty(lib.sparton_sparse_workspace_size(B, V), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(lib.sparton_sparse_workspace_size(B, V), dtype=torch.uint8, device="cuda")
     sh = torch.cuda.current_stream().cuda_stream
     assert lib.sparton_reps_csr(r.data_ptr(), 1, B, V, 0.0, crow.data_ptr(), cols.data_ptr(),
                                 vals.data_ptr(), cap, ws.data_ptr(), ws.numel(), sh) == 0
