@@ -33,8 +33,10 @@ bounded sample of the same workload.
 
 Further legs (``--legs``), reported as objects in the same line: ``losses``
 (InfoNCE and the fused regularisers on reps-shaped input), ``sparse`` (CSR and
-top-k of reps), ``transform`` (the MLM transform's kernels and SpartonProjection
-forward + backward).
+top-k of reps), ``transform`` (the MLM transform's kernels, its dense GEMMs and
+SpartonProjection forward + backward). Each leg call is timed with CUDA events
+after an L2 flush and a short spin kernel (``preroll``), so that its span holds
+the call's GPU work rather than Python's queueing ahead of it.
 
 ``--impl reference`` times that CPU reference alone (rank 0; other ranks exit)
 and prints its line with ``"impl": "reference"``.
@@ -84,6 +86,13 @@ def log(*a):
 
 def nominal_flops(c) -> float:
     return 4.0 * c["B"] * c["S"] * c["D"] * c["V"]
+
+
+def preroll() -> None:
+    """A ~0.1 ms spin kernel queued between the L2 flush and a leg's start event:
+    the GPU stays busy while Python queues the call under test, so the timed
+    span holds that call's GPU work, not the host's launch latency before it."""
+    torch.cuda._sleep(200_000)
 
 
 def make_inputs(c, seed=0):
@@ -396,6 +405,7 @@ def run_losses(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
         barrier()
         for e0, e1 in evs:
             flush.zero_()
+            preroll()
             e0.record(stream)
             fn()
             e1.record(stream)
@@ -475,6 +485,7 @@ def run_sparse(args, c, dev, group, world, Vs, flush, stream, barrier, max_over_
         barrier()
         for e0, e1 in evs:
             flush.zero_()
+            preroll()
             e0.record(stream)
             fn()
             e1.record(stream)
@@ -557,6 +568,7 @@ def run_transform(args, c, dev, group, world, Vs, flush, stream, barrier, max_ov
         barrier()
         for e0, e1 in evs:
             flush.zero_()
+            preroll()
             e0.record(stream)
             fn()
             e1.record(stream)
