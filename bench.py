@@ -612,9 +612,11 @@ def main(argv=None) -> int:
                     help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
                     help="stream priority of the NCCL process group (N > 1)")
-    ap.add_argument("--hidden-reduce", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--hidden-reduce", choices=["peer", "nccl", "rsag"], default="peer",
                     help="N > 1: sum of the partial d_hidden over NVLink peer memory (packed "
-                         "rows only) or NCCL all-reduce of all rows in chunks")
+                         "rows only), NCCL all-reduce of all rows in chunks, or per chunk an "
+                         "fp32 NCCL reduce-scatter and an all-gather of the parts rounded to "
+                         "hidden's dtype (rsag)")
     ap.add_argument("--legs", default="device,e2e,cpu,losses,sparse,transform",
                     help="comma list of legs: device (value), e2e, cpu (baseline), losses "
                          "(training losses on the head's output), sparse (CSR / top-k of "
@@ -691,7 +693,9 @@ def main(argv=None) -> int:
         peer = PeerHiddenReduce.get(group, dev, B * S, D, c["dtype"])
     import sparton_b200.head as head_mod
 
-    head_mod.HIDDEN_REDUCE = args.hidden_reduce  # the e2e leg's SpartonHead does the same
+    # the e2e leg's SpartonHead does the same
+    head_mod.HIDDEN_REDUCE = "nccl" if args.hidden_reduce == "rsag" else args.hidden_reduce
+    head_mod.REDUCE_SCATTER_GATHER = args.hidden_reduce == "rsag"
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
     def step(k0=None, k1=None):
