@@ -903,7 +903,9 @@ def main(argv=None) -> int:
         try:
             # A bounded run of the same per-step work as the reference arm
             # (--impl reference): whole batch where it fits, same inputs.
-            res = cpu_baseline(c, cpu_rows_for(c, args.cpu_rows), steps=3, warmup=1)
+            # Three warm-up steps, as the reference arm takes at its minimum
+            # --warmup: the first steps of the CPU head fault in its buffers.
+            res = cpu_baseline(c, cpu_rows_for(c, args.cpu_rows), steps=3, warmup=3)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample",
                                                         "cpu_model")}
         except Exception as e:  # pragma: no cover
