@@ -16,8 +16,9 @@
 //   "cols" (MN-major): A as [K][M], B as [K][N]: the output index is
 //                     contiguous, as for dx = dy @ W (B = W [K=N_out][N=K_in])
 //                     or dW = dy.T @ x (A = dy [K][M], B = x [K][N]).
-// TMA loads either form with 128-byte swizzle: a K-major tile is one box of
-// [rows x 64 k]; an MN-major tile is boxes of [64 rows (contiguous) x 64 k]
+// TMA loads either form with 128-byte swizzle: a K-major tile is boxes of
+// [64 rows x 64 k] 8 KB apart (one swizzled [rows x 64 k] tile); an MN-major
+// tile is boxes of [64 rows (contiguous) x 64 k]
 // placed 8 KB apart, which is the canonical MN-major layout the tcgen05 shared
 // memory descriptor describes with leading byte offset 8 KB (between 64-element
 // MN blocks) and stride byte offset 1 KB (between groups of 8 k).
@@ -124,19 +125,26 @@ __device__ __forceinline__ void load_stage(const CUtensorMap* tmA, const CUtenso
                                            uint32_t a_dst, uint32_t full, const UnitPos& u,
                                            int kb, int bn) {
   const int k0 = kb * kBK;
-  if (kAmn) {
+  // Both layouts arrive as 64-row (or 64-column) boxes of 8 KB: a K-major box
+  // of 64 rows x 64 k is 8 row groups of 1 KB, so consecutive boxes form the
+  // same swizzled tile as one tall box, and several boxes keep the copy engine
+  // busy in parallel.
 #pragma unroll
-    for (int i = 0; i < kBM / 64; ++i) tma_load_2d(a_dst + i * kBoxBytes, tmA, full, u.m0 + 64 * i, k0);
-  } else {
-    tma_load_2d(a_dst, tmA, full, k0, u.m0);
+  for (int i = 0; i < kBM / 64; ++i) {
+    if (kAmn)
+      tma_load_2d(a_dst + i * kBoxBytes, tmA, full, u.m0 + 64 * i, k0);
+    else
+      tma_load_2d(a_dst + i * kBoxBytes, tmA, full, k0, u.m0 + 64 * i);
   }
   const uint32_t b_dst = a_dst + kABytes;
-  if (kBmn) {
 #pragma unroll
-    for (int i = 0; i < kBN / 64; ++i)
-      if (64 * i < bn) tma_load_2d(b_dst + i * kBoxBytes, tmB, full, u.n0 + 64 * i, k0);
-  } else {
-    tma_load_2d(b_dst, tmB, full, k0, u.n0);
+  for (int i = 0; i < kBN / 64; ++i) {
+    if (64 * i < bn) {
+      if (kBmn)
+        tma_load_2d(b_dst + i * kBoxBytes, tmB, full, u.n0 + 64 * i, k0);
+      else
+        tma_load_2d(b_dst + i * kBoxBytes, tmB, full, k0, u.n0 + 64 * i);
+    }
   }
 }
 
@@ -274,6 +282,44 @@ __device__ __forceinline__ void store_row_chunk(const GemmParams& p, int m, int 
   }
 }
 
+// Stores the warp's 32 rows x 32 columns (lane l holds row `l` of the chunk,
+// starting at base; rows ld elements apart, 16-byte aligned) through a shared
+// tile so that each store instruction writes whole 16-byte segments of a few
+// rows (8 rows of 64 bytes for 16-bit O, 4 of 128 for fp32) instead of one
+// segment of 32 rows: full sectors and a quarter of the L2 write requests.
+// The tile's segments are XOR-swizzled by row (no more than 2-way bank
+// conflicts). Warp-collective; rows at or past rows_valid are not written.
+template <typename O>
+__device__ __forceinline__ void store_chunk_rows(O* base, long long ld, int rows_valid,
+                                                 uint8_t* tile, const float (&v)[32], int lane) {
+  constexpr int kRowBytes = 32 * static_cast<int>(sizeof(O));
+  constexpr int kSeg = kRowBytes / 16;   // 16-byte segments per row
+  constexpr int kRowsPer = 32 / kSeg;    // rows per store instruction
+  constexpr int kPer = 16 / static_cast<int>(sizeof(O));  // values per segment
+#pragma unroll
+  for (int sg = 0; sg < kSeg; ++sg) {
+    uint4 w;
+    uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+    if constexpr (sizeof(O) == 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wp[j] = __float_as_uint(v[sg * kPer + j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wp[j] = pack2<O>(v[sg * kPer + 2 * j], v[sg * kPer + 2 * j + 1]);
+    }
+    *reinterpret_cast<uint4*>(tile + lane * kRowBytes + 16 * (sg ^ (lane % kSeg))) = w;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < kSeg; ++q) {
+    const int r = q * kRowsPer + lane / kSeg, sg = lane % kSeg;
+    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * kRowBytes + 16 * (sg ^ (r % kSeg)));
+    if (r < rows_valid)
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(base + r * ld) + 16 * sg) = w;
+  }
+  __syncwarp();
+}
+
 // Stores the warp's 32 rows x 32 columns (lane l holds row m0 + l) through a
 // shared tile, one row per step by consecutive lanes: coalesced stores for
 // outputs whose rows are not 16-byte aligned (C with an odd row length).
@@ -295,29 +341,37 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
                              int lane, float* stage_tile, T* sbias) {
   const int quad = warp & 3;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+  const bool has_bias = p.bias != nullptr && p.splits == 1;
+  // The bias of unit u's columns, 8 per lane (lane l: columns 8l .. 8l + 7 of
+  // the tile; zero past N), fetched one tile ahead so that its load overlaps
+  // the wait for the accumulator.
+  auto fetch_bias = [&](long long u) -> uint4 {
+    uint4 r = make_uint4(0u, 0u, 0u, 0u);
+    if (!has_bias || u >= p.units) return r;
+    const int n0 = unit_pos(p, u).n0;
+    const int nb = min(p.bn, p.N - n0), j = lane * 8;
+    const T* bsrc = static_cast<const T*>(p.bias) + n0 + j;
+    if (p.vec_bias && j + 8 <= nb) return __ldg(reinterpret_cast<const uint4*>(bsrc));
+    T* e = reinterpret_cast<T*>(&r);
+    for (int i = 0; i < 8; ++i)
+      if (j + i < nb) e[i] = bsrc[i];
+    return r;
+  };
+  uint4 bias_next = fetch_bias(blockIdx.x);
   uint32_t tile = 0;
   for (long long u = blockIdx.x; u < p.units; u += gridDim.x) {
     const UnitPos up = unit_pos(p, u);
     const int acc = tile % kNumAcc;
     const uint32_t aph = (tile / kNumAcc) & 1;
-    if (p.bias != nullptr && p.splits == 1) {
-      // this tile's bias into the warp's shared copy (8 values per lane)
-      const T* bsrc = static_cast<const T*>(p.bias) + up.n0;
-      const int nb = min(p.bn, p.N - up.n0);
-      __syncwarp();  // the previous tile's reads of sbias are done
-      const int j = lane * 8;
-      if (j < nb) {
-        if (p.vec_bias && j + 8 <= nb) {
-          *reinterpret_cast<uint4*>(sbias + j) = __ldg(reinterpret_cast<const uint4*>(bsrc + j));
-        } else {
-          for (int i = 0; i < 8 && j + i < nb; ++i) sbias[j + i] = bsrc[j + i];
-        }
-      }
-      __syncwarp();
-    }
     const bool got = mbar_wait_bounded(c.bar(kBarTFull + acc), aph, c.abort_flag, p.status,
                                        SPARTON_DEV_TIMEOUT_EPILOGUE);
     if (!__all_sync(0xFFFFFFFFu, got)) break;
+    if (has_bias) {
+      // this tile's bias into the warp's shared copy, the next tile's on its way
+      *reinterpret_cast<uint4*>(sbias + lane * 8) = bias_next;
+      __syncwarp();
+      bias_next = fetch_bias(u + gridDim.x);
+    }
     tc_fence_after_sync();
     const int m = up.m0 + quad * 32 + lane;
     const int nch = (min(p.bn, p.N - up.n0) + 31) >> 5;
@@ -333,12 +387,12 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
       const int cnt = min(32, p.N - n);
       if (p.splits > 1) {
         // (no early exit: the TMEM load of the next chunk is warp-collective)
+        const int m0w = up.m0 + quad * 32;  // the warp's first row
         float* dst = p.partial + (static_cast<size_t>(up.split) * p.M + (row_ok ? m : 0)) * p.N + n;
-        if (!row_ok) {
-        } else if (p.vec_partial && cnt == 32) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        if (p.vec_partial && cnt == 32) {
+          store_chunk_rows<float>(p.partial + (static_cast<size_t>(up.split) * p.M + m0w) * p.N + n,
+                                  p.N, p.M - m0w, reinterpret_cast<uint8_t*>(stage_tile), v, lane);
+        } else if (!row_ok) {
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -346,12 +400,21 @@ __device__ void run_epilogue(const GemmParams& p, uint32_t tmem_base, const Ctrl
         }
       } else {
         if (p.bias != nullptr) {
-          const T* bp = sbias + 32 * ch;  // shared copy, the same address in every lane
+          // shared copy, the same addresses in every lane (broadcast reads)
+          const uint4* bp = reinterpret_cast<const uint4*>(sbias + 32 * ch);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < cnt) v[i] += to_f32<T>(bp[i]);
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w = bp[q];
+            const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * q + i] += to_f32<T>(e[i]);
+          }
         }
-        if (p.vec_store) {
+        if (p.vec_store && cnt == 32) {
+          const int m0w = up.m0 + quad * 32;
+          store_chunk_rows<O>(static_cast<O*>(p.C) + static_cast<size_t>(m0w) * p.ldc + n, p.ldc,
+                              p.M - m0w, reinterpret_cast<uint8_t*>(stage_tile), v, lane);
+        } else if (p.vec_store) {
           if (row_ok) store_row_chunk<O>(p, m, n, v);
         } else {
           store_chunk_staged<O>(p, stage_tile, up.m0 + quad * 32, n, v, lane);
@@ -528,9 +591,9 @@ int launch_typed(CUtensorMapDataType dt, const GemmArgs& a, cudaStream_t stream)
   p.vec_bias = reinterpret_cast<uintptr_t>(a.bias) % 16 == 0;
   p.vec_partial = a.N % 4 == 0;
   CUtensorMap tmA, tmB;
-  int st = make_operand_map(&tmA, dt, a.A, kAmn, a.M, a.K, a.lda, kBM);
+  int st = make_operand_map(&tmA, dt, a.A, kAmn, a.M, a.K, a.lda, 64);
   if (st != SPARTON_OK) return st;
-  st = make_operand_map(&tmB, dt, a.B, kBmn, a.N, a.K, a.ldb, p.bn);
+  st = make_operand_map(&tmB, dt, a.B, kBmn, a.N, a.K, a.ldb, 64);
   if (st != SPARTON_OK) return st;
 
   static std::mutex mu;
