@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "dtype.cuh"
 #include "internal.h"
@@ -157,55 +158,72 @@ __global__ void __launch_bounds__(kRegWarps * 32)
   }
 }
 
-// grad over the flattened [B * V]: kPer consecutive elements per thread and
-// step (16-byte loads and stores when reps and grad are 16-byte aligned, else
-// kPer = 1); the column index advances with the element and wraps at V.
+// grad over the flattened [B * V]: thread t takes kU vectors of kPer
+// consecutive elements (vector t + i * stride, i < kU; 16-byte loads and stores
+// when reps and grad are 16-byte aligned, else kPer = 1), all kU loads issued
+// before any is used; the column index advances with the element and wraps
+// at V. The last n % kPer elements go to block 0's first threads.
+constexpr int kBwdU = 4;
 template <typename T, int kPer>
 __global__ void __launch_bounds__(256)
     reg_bwd_kernel(const T* __restrict__ reps, const float* __restrict__ colsum,
                    const float* __restrict__ g_l1, const float* __restrict__ g_flops,
                    float scale_l1, float scale_flops, long long n, int V, T* __restrict__ grad) {
-  const float c0 = g_l1 != nullptr ? __ldg(g_l1) * scale_l1 : 0.f;
-  const float c1 = g_flops != nullptr ? __ldg(g_flops) * scale_flops : 0.f;
   const long long nvec = n / kPer;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  long long vi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  // the column of the thread's first element, and how far it moves per step
-  // (one division each per thread; 32-bit when the offsets fit)
-  int vcol, vstep;
-  if (n <= 0xFFFFFFFFll) {
-    vcol = static_cast<int>(static_cast<unsigned>(vi * kPer) % static_cast<unsigned>(V));
-    vstep = static_cast<int>(static_cast<unsigned>(stride * kPer) % static_cast<unsigned>(V));
-  } else {
-    vcol = static_cast<int>((vi * kPer) % V);
-    vstep = static_cast<int>((stride * kPer) % V);
-  }
-  for (; vi < nvec; vi += stride) {
-    const long long g = vi * kPer;
-    int v = vcol;
-    vcol += vstep;
-    if (vcol >= V) vcol -= V;
-    if constexpr (kPer == 1) {
-      const float x = ldg_f32<T>(reps + g);
-      const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-      grad[g] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
-    } else {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(reps + g));
-      const T* e = reinterpret_cast<const T*>(&w);
-      uint4 o;
-      T* oe = reinterpret_cast<T*>(&o);
+  const long long v0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  using Vec = typename std::conditional<kPer == 1, T, uint4>::type;
+  Vec w[kBwdU];
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const float x = to_f32<T>(e[i]);
-        const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-        oe[i] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
-        if (++v == V) v = 0;
-      }
-      *reinterpret_cast<uint4*>(grad + g) = o;
+  for (int i = 0; i < kBwdU; ++i) {
+    const long long vi = v0 + i * stride;
+    if (vi < nvec) {
+      if constexpr (kPer == 1)
+        w[i] = reps[vi];
+      else
+        w[i] = __ldg(reinterpret_cast<const uint4*>(reps) + vi);
     }
   }
+  const float c0 = g_l1 != nullptr ? __ldg(g_l1) * scale_l1 : 0.f;
+  const float c1 = g_flops != nullptr ? __ldg(g_flops) * scale_flops : 0.f;
+  // the column of the thread's first element, and how far it moves per vector
+  // (32-bit divisions when the offsets fit)
+  int vcol, vstep;
+  if (n <= 0xFFFFFFFFll) {
+    vcol = static_cast<int>(static_cast<unsigned>(v0 * kPer) % static_cast<unsigned>(V));
+    vstep = static_cast<int>(static_cast<unsigned>(stride * kPer) % static_cast<unsigned>(V));
+  } else {
+    vcol = static_cast<int>((v0 * kPer) % V);
+    vstep = static_cast<int>((stride * kPer) % V);
+  }
+#pragma unroll
+  for (int i = 0; i < kBwdU; ++i) {
+    const long long vi = v0 + i * stride;
+    if (vi < nvec) {
+      int v = vcol;
+      if constexpr (kPer == 1) {
+        const float x = to_f32<T>(w[i]);
+        const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+        grad[vi] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
+      } else {
+        const T* e = reinterpret_cast<const T*>(&w[i]);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const float x = to_f32<T>(e[k]);
+          const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+          oe[k] = from_f32<T>(fmaf(c0, s, c1 * __ldg(colsum + v)));
+          if (++v == V) v = 0;
+        }
+        *reinterpret_cast<uint4*>(grad + vi * kPer) = o;
+      }
+    }
+    vcol += vstep;
+    if (vcol >= V) vcol -= V;
+  }
   // the last n % kPer elements
-  const long long t = nvec * kPer + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long t = nvec * kPer + v0;
   if (kPer > 1 && t < n && blockIdx.x == 0) {
     const float x = ldg_f32<T>(reps + t);
     const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
@@ -244,9 +262,8 @@ int launch_bwd_typed(const void* reps, const float* colsum, const float* g_l1,
   const bool vec = reinterpret_cast<uintptr_t>(reps) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(grad) % 16 == 0;
   const long long units = vec ? n / kPer : n;
-  // 4 blocks per SM; every thread takes a few vectors
-  const long long blocks =
-      std::max(1ll, std::min((units + 255) / 256, 4ll * device_sm_count()));
+  // every thread takes kBwdU vectors (the grid covers all of them in one pass)
+  const long long blocks = std::max(1ll, (units + 256ll * kBwdU - 1) / (256ll * kBwdU));
   if (vec)
     reg_bwd_kernel<T, kPer><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         static_cast<const T*>(reps), colsum, g_l1, g_flops, scale_l1, scale_flops, n, V,

@@ -222,7 +222,6 @@ __global__ void __launch_bounds__(kCsrThreads)
           s_fail = 1;
           break;
         }
-        __nanosleep(32);
         f = lb_read(flags + j);
       }
     }
