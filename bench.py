@@ -698,7 +698,11 @@ def main(argv=None) -> int:
     head_mod.REDUCE_SCATTER_GATHER = args.hidden_reduce == "rsag"
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
-    def step(k0=None, k1=None):
+    # sharded backward phases of the timed steps (events on the streams that run
+    # them): dH partial done, d_hidden reduction done, dW / db done
+    phase_ev = []
+
+    def step(k0=None, k1=None, ph=None):
         _lib.check(lib.sparton_mask_prepare(md.data_ptr(), 2, B, S, wsf.data_ptr(), wsf.numel(), sh),
                    "mask_prepare")
         if k0 is not None:
@@ -733,12 +737,18 @@ def main(argv=None) -> int:
                                        peer.partial(B, S).data_ptr(), None, None,
                                        _lib.DTYPE[torch.float32], dt, wsb.data_ptr(),
                                        wsb.numel(), sh), "bwd dH")
+            if ph is not None:
+                ph[0].record(stream)
             side.wait_stream(stream)
             _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(),
                                        Hd.data_ptr(), Wd.data_ptr(), dt, B, S, D, Vs, None,
                                        dW.data_ptr(), _lib.ptr(db), _lib.DTYPE[dh_dtype], dt,
                                        wsb.data_ptr(), wsb.numel(), side.cuda_stream), "bwd dW")
+            if ph is not None:
+                ph[2].record(side)
             peer.reduce(wsf, B, S, dH)
+            if ph is not None:
+                ph[1].record(stream)
             stream.wait_stream(side)
             return
         # Sharded, with SpartonHead's sharded backward schedule: partial dH in
@@ -753,11 +763,17 @@ def main(argv=None) -> int:
                                        _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(), wsb.numel(), sh),
                        "bwd dH")
             red.reduce(b0, b1)
+        if ph is not None:
+            ph[0].record(stream)
         _lib.check(lib.sparton_bwd(gd.data_ptr(), reps.data_ptr(), idx.data_ptr(), Hd.data_ptr(),
                                    Wd.data_ptr(), dt, B, S, D, Vs, None, dW.data_ptr(),
                                    _lib.ptr(db), _lib.DTYPE[dh_dtype], dt, wsb.data_ptr(),
                                    wsb.numel(), sh), "bwd dW")
+        if ph is not None:
+            ph[2].record(stream)
         red.finish()
+        if ph is not None:
+            ph[1].record(stream)
 
     def barrier():
         if world > 1:
@@ -782,13 +798,28 @@ def main(argv=None) -> int:
     kern_ev = [(ev(), ev()) for _ in range(args.steps)]
     sampler = ClockSampler(dev)
     barrier()
+    if world > 1:
+        phase_ev = [(ev(), ev(), ev()) for _ in range(args.steps)]
     with sampler:
         for i in range(args.steps):
             flush.zero_()
             step_ev[i][0].record(stream)
-            step(*kern_ev[i])
+            step(*kern_ev[i], ph=phase_ev[i] if phase_ev else None)
             step_ev[i][1].record(stream)
         barrier()
+    bwd_phases = None
+    if phase_ev:
+        # from the end of the forward kernel: dH partial (dH gather and sort) done;
+        # then from that point: the d_hidden reduction done, dW / db done
+        n = args.steps
+        bwd_phases = {
+            "dh_partial_ms": round(max_over_ranks(
+                sum(kern_ev[i][1].elapsed_time(phase_ev[i][0]) for i in range(n)) / n), 4),
+            "reduce_after_dh_ms": round(max_over_ranks(
+                sum(phase_ev[i][0].elapsed_time(phase_ev[i][1]) for i in range(n)) / n), 4),
+            "dw_after_dh_ms": round(max_over_ranks(
+                sum(phase_ev[i][0].elapsed_time(phase_ev[i][2]) for i in range(n)) / n), 4),
+        }
     step_ms = max_over_ranks(sum(a.elapsed_time(e) for a, e in step_ev) / args.steps)
     kern_ms = sum(a.elapsed_time(e) for a, e in kern_ev) / args.steps
     kern_ms_max = max_over_ranks(kern_ms)
@@ -882,6 +913,7 @@ def main(argv=None) -> int:
         "fwd_kernel_ms": round(kern_ms_max, 4),
         "fwd_ms": round(fwd_part_ms, 4),
         "bwd_ms": round(bwd_part_ms, 4),
+        "bwd_phases": bwd_phases,
         "fwd_inference_ms": round(inf_ms, 4),
         "roofline": {"kernel": "fwd_tc_kernel", "bound": "tensor", "achieved": round(achieved, 2),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),

@@ -725,14 +725,25 @@ __global__ void __launch_bounds__(kRowThreads)
           *reinterpret_cast<uint4*>(skey + vi * kPer) =
               make_uint4(key[u][0], key[u][1], key[u][2], key[u][3]);
         }
+        const int off0 = vi * kPer;
+        if (off0 >= lo && off0 + kPer <= hi) {  // a whole vector of the row
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) {
-          const int off = vi * kPer + e;
-          if (off >= lo && off < hi) {
+          for (int e = 0; e < kPer; ++e) {
             if (key[u][e] == kZeroKey)
               ++zc;
             else
               atomicAdd(&hist[key[u][e] >> shift0], 1u);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) {
+            const int off = off0 + e;
+            if (off >= lo && off < hi) {
+              if (key[u][e] == kZeroKey)
+                ++zc;
+              else
+                atomicAdd(&hist[key[u][e] >> shift0], 1u);
+            }
           }
         }
       }
@@ -813,19 +824,46 @@ __global__ void __launch_bounds__(kRowThreads)
 
   // ---- 3. the list
   if (cge <= static_cast<uint32_t>(kRowList)) {
-    // every entry with key >= prefix (lower bits of prefix are 0)
-    for (int off0 = lo + 32 * (threadIdx.x >> 5); off0 < hi; off0 += kRowThreads) {
-      const int off = off0 + lane;
-      const uint32_t key = off < hi ? static_cast<uint32_t>(skey[off]) : 0u;
-      const bool take = off < hi && key >= prefix;
-      const unsigned m = __ballot_sync(0xFFFFFFFFu, take);
-      if (m == 0u) continue;
+    // every entry with key >= prefix (lower bits of prefix are 0): a lane
+    // checks one staged vector of kPer keys, the warp reserves its slots with
+    // one shared atomic
+    const int warp = threadIdx.x >> 5;
+    for (int base = 32 * warp; base < nvec; base += kRowThreads) {
+      const int vi = base + lane;
+      uint32_t key[kPer];
+      unsigned take = 0u;
+      if (vi < nvec) {
+        if constexpr (kPer == 1) {
+          key[0] = skey[vi];
+        } else if constexpr (sizeof(KeyT) == 2) {
+          const uint4 w = *reinterpret_cast<const uint4*>(skey + vi * kPer);
+          const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            key[2 * e] = q[e] & 0xFFFFu;
+            key[2 * e + 1] = q[e] >> 16;
+          }
+        } else {
+          const uint4 w = *reinterpret_cast<const uint4*>(skey + vi * kPer);
+          key[0] = w.x, key[1] = w.y, key[2] = w.z, key[3] = w.w;
+        }
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const int off = vi * kPer + e;
+          if (off >= lo && off < hi && key[e] >= prefix) take |= 1u << e;
+        }
+      }
+      int wtot;
+      const int ex = warp_excl_scan(__popc(take), lane, wtot);
+      if (wtot == 0) continue;  // (warp-uniform)
       uint32_t at = 0;
-      if (lane == 0) at = atomicAdd(&s_n, static_cast<uint32_t>(__popc(m)));
-      at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(m & ((1u << lane) - 1u));
-      if (take)
-        list[at] = (static_cast<unsigned long long>(key) << 32) |
-                   (0xFFFFFFFFu - static_cast<uint32_t>(off - lo));
+      if (lane == 0) at = atomicAdd(&s_n, static_cast<uint32_t>(wtot));
+      at = __shfl_sync(0xFFFFFFFFu, at, 0) + ex;
+#pragma unroll
+      for (int e = 0; e < kPer; ++e)
+        if ((take >> e) & 1u)
+          list[at++] = (static_cast<unsigned long long>(key[e]) << 32) |
+                       (0xFFFFFFFFu - static_cast<uint32_t>(vi * kPer + e - lo));
     }
   } else {
     // K = prefix exactly: the entries above K, then the first `remaining`
@@ -866,16 +904,26 @@ __global__ void __launch_bounds__(kRowThreads)
   }
   __syncthreads();
 
-  // ---- 4. rank = entries before this one; rank < k goes to the output
+  // ---- 4. rank = entries before this one; rank < k goes to the output.
+  // With a short list, tpe consecutive lanes share an entry, each counting
+  // over a part of the list, and add their counts.
   const int m = static_cast<int>(s_n);
-  for (int t = threadIdx.x; t < m; t += kRowThreads) {
-    const unsigned long long c = list[t];
+  const int tpe = m <= kRowThreads / 4 ? 4 : (m <= kRowThreads / 2 ? 2 : 1);
+  for (int t0 = 0; t0 < m * tpe; t0 += kRowThreads) {
+    const int t = t0 + static_cast<int>(threadIdx.x);
+    const int i = t / tpe, part = t % tpe;
+    const bool valid = i < m;
+    const unsigned long long c = valid ? list[i] : 0ull;
     int rank = 0;
-    int j = 0;
-    for (; j + 4 <= m; j += 4)
-      rank += (list[j] > c) + (list[j + 1] > c) + (list[j + 2] > c) + (list[j + 3] > c);
-    for (; j < m; ++j) rank += list[j] > c;
-    if (rank < k) {
+    if (valid) {
+      const int j1 = (part + 1) * m / tpe;
+      int j = part * m / tpe;
+      for (; j + 4 <= j1; j += 4)
+        rank += (list[j] > c) + (list[j + 1] > c) + (list[j + 2] > c) + (list[j + 3] > c);
+      for (; j < j1; ++j) rank += list[j] > c;
+    }
+    for (int o = 1; o < tpe; o <<= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, o);
+    if (valid && part == 0 && rank < k) {
       const int v = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(c));
       out_idx[static_cast<size_t>(b) * k + rank] = v;
       out_vals[static_cast<size_t>(b) * k + rank] = row[v];

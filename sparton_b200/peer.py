@@ -6,7 +6,10 @@ rank allocates three buffers: its fp32 partial d_hidden (written by its own
 backward), its reduced-row buffer and its flag words. At set-up the ranks
 exchange CUDA IPC handles of those buffers through the process group (once,
 for a given capacity) and map each other's; from then on a reduction is four
-kernel launches on the calling stream and no host synchronisation:
+kernel launches and no host synchronisation, on the instance's own stream at the
+device's highest priority (ordered after the calling stream's work so far and
+before its later work), so that they are not queued behind kernels the caller
+runs beside them:
 
 * only the packed rows (positions before each batch row's extent, counted on
   the device by the forward) cross NVLink, where a library collective would
@@ -105,6 +108,9 @@ class PeerHiddenReduce:
                                  self.flags.data_ptr()))
                 else:
                     ptrs.append(tuple(_open(h, off) for h, off in bufs))
+        # The reduction's own stream, at the device's highest priority: its
+        # short kernels get SMs ahead of the d_weight blocks queued beside it.
+        self.stream = torch.cuda.Stream(device=device, priority=-1)
         arr = ctypes.c_void_p * self.world
         self._parts = arr(*[p[0] for p in ptrs])
         self._reds = arr(*[p[1] for p in ptrs])
@@ -117,9 +123,13 @@ class PeerHiddenReduce:
 
     def reduce(self, fwd_workspace: torch.Tensor, B: int, S: int, out: torch.Tensor) -> None:
         """out [B, S, D] (hidden's dtype) = sum over the ranks of their partials,
-        on the current stream; every rank calls it once per backward."""
+        ordered after the current stream's work and before its later work (the
+        kernels run on the reduction's high-priority stream); every rank calls
+        it once per backward."""
         self.epoch += 1
         lib = _lib.load()
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
         with torch.cuda.device(self.device):
             st = lib.sparton_hidden_allreduce(ctypes.cast(self._parts, ctypes.c_void_p),
                                               ctypes.cast(self._reds, ctypes.c_void_p),
@@ -128,8 +138,11 @@ class PeerHiddenReduce:
                                               self.world, self.epoch, fwd_workspace.data_ptr(),
                                               B, S, self.D, out.data_ptr(),
                                               _lib.DTYPE[out.dtype], self.status.data_ptr(),
-                                              _lib.stream_handle(self.device))
+                                              self.stream.cuda_stream)
         _lib.check(st, "sparton_hidden_allreduce")
+        out.record_stream(self.stream)
+        fwd_workspace.record_stream(self.stream)
+        cur.wait_stream(self.stream)
 
     def device_status(self) -> int:
         """SPARTON_DEV_TIMEOUT_PEER (0x105) if a wait on a peer gave up (synchronises)."""
