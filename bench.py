@@ -295,7 +295,9 @@ def run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier, 
     is refilled only after the step that read it has finished. Every step's
     copies, its L2 flush and its compute lie inside the timed region, which runs
     from before the first copy to after the last read-back; time per step is
-    that span / steps."""
+    that span / steps. The parameters' gradients are set to None before each
+    backward, as a training loop's zero_grad does (and the reference arm's
+    torch head every step), so each backward writes them instead of adding."""
     from sparton_b200.head import SpartonHead
 
     from torch import nn
@@ -311,6 +313,7 @@ def run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier, 
             decoder.bias.copy_(b)
     head = SpartonHead(V, D, use_bias=c["bias"], process_group=group).to(dev, c["dtype"])
     head.tie_weights(decoder)
+    params = list(head.parameters()) + list(decoder.parameters())
     H_pin, m_pin, g_pin = H.pin_memory(), mask.pin_memory(), gs.pin_memory()
     H_dev = [torch.empty_like(H, device=dev) for _ in range(2)]
     m_dev = [torch.empty_like(mask, device=dev) for _ in range(2)]
@@ -344,6 +347,8 @@ def run_e2e(args, c, dev, group, W, b, H, mask, gs, Vs, flush, stream, barrier, 
             flush.zero_()
             stream.wait_event(copied[k])
             hid = H_dev[k].detach().requires_grad_(True)
+            for prm in params:  # a training loop's zero_grad(set_to_none=True), as the
+                prm.grad = None  # reference arm's torch head does every step
             out = head(hid, m_dev[k])
             out.backward(g_dev[k])
             done = torch.cuda.Event()
