@@ -263,7 +263,7 @@ int sparton_reps_topk(const void* reps, int dtype, int64_t B, int64_t V, int64_t
 /* --------------------------------------------------------- MLM transform */
 /* The GELU + LayerNorm part of the MLM transform in front of the head
  * (training/model.py:25-35, BERT's predictions.transform): with y = x @ Wd^T
- * + bd from the dense layer (a plain GEMM, left to the caller's BLAS),
+ * + bd from the dense layer (a plain GEMM: sparton_gemm below, or the caller's BLAS),
  *   h = LayerNorm(gelu(y)) * gamma + beta   (exact erf gelu, its output
  *   rounded to `dtype`; biased variance; eps as torch.nn.LayerNorm)
  * for y, h [rows, D] in `dtype` and gamma, beta [D]; mean / rstd [rows] fp32
@@ -276,8 +276,8 @@ int sparton_transform_fwd(const void* y, const void* gamma, const void* beta, fl
 size_t sparton_transform_workspace_size(int64_t rows, int64_t D);
 
 /* Backward of sparton_transform_fwd from dh [rows, D] (the head's d_hidden):
- * dy [rows, D] = d(gelu + LayerNorm)/dy (the caller's BLAS then forms
- * dx = dy @ Wd and dWd = dy^T @ x), and, each optional (NULL skips it),
+ * dy [rows, D] = d(gelu + LayerNorm)/dy (sparton_gemm or the caller's BLAS then
+ * forms dx = dy @ Wd and dWd = dy^T @ x), and, each optional (NULL skips it),
  * d_gamma, d_beta [D] and d_bias [D] = sum over rows of dy (the dense bias),
  * in `dtype`, summed in a fixed order (rows <= 65535 * 256 when any of them
  * is requested). */
