@@ -4,13 +4,13 @@
                     [--workload config2|config3|config4|config5]
     (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
 
-Default workload (the configuration its metric is
-quoted on): B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden
+Default workload (benchmark configuration 2, the one the metric is quoted
+on): B=128, S=256, D=768, V=30522, bf16 with fp32 accumulation, hidden
 ~ N(0,1), W ~ N(0,0.02), bias ~ N(0,0.02), right-padded mask with lengths
 U[32,256], upstream grad g ~ N(0,1); seeded synthetic data standing in for
-SPLADE batches. ``--workload`` selects the other BASELINE configurations
+SPLADE batches. ``--workload`` selects the other benchmark configurations
 (WORKLOADS below: config 3 V=250002, config 4 fp16 B=512 S=512, config 5
-D=4096 V=128256 without bias), same distributions as BASELINE.json states.
+D=4096 V=128256 without bias), with the same distributions.
 With N GPUs the decoder is vocabulary-sharded over the ranks (the same total
 workload: strong scaling) and the partial d_hidden is all-reduced (fp32, NCCL,
 in chunks of batch rows overlapping the backward; high-priority NCCL streams).
@@ -19,7 +19,7 @@ One step = head forward (mask reduction + fused GEMM/max/argmax/log1p kernel)
 + backward (sort by argmax, dH, dW, db; single GPU: the dH and dW halves on two
 streams) [+ all-reduce of dH].
 
-Prints ONE JSON line on rank 0. ``value`` is the BASELINE metric, nominal
+Prints ONE JSON line on rank 0. ``value`` is the benchmark's metric, nominal
 fwd+bwd TFLOP/s = 4*B*S*D*V / step time, with inputs resident in HBM and the
 L2 flushed (256 MiB write) before every timed step; time is the max over ranks
 of CUDA-event time. ``e2e`` is the same metric through the public module
@@ -58,7 +58,7 @@ if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
 METRIC = "fused head fwd+bwd TFLOP/s (4·B·S·D·V) & tokens/s at 1/2/4/8 B200; % of bf16 peak"
-# BASELINE.json configs[1..4] ("config 2" .. "config 5"). Config 2 is the one the
+# The benchmark configurations "config 2" .. "config 5". Config 2 is the one the
 # metric is quoted on and the default; the others are selected with --workload.
 WORKLOADS = {
     "config2": dict(name="config 2 (BERT-base SPLADE head)", B=128, S=256, D=768, V=30522,
@@ -213,8 +213,8 @@ def cpu_model() -> str:
 def cpu_rows_for(c, rows=None) -> int:
     """Batch rows one CPU step runs: the whole batch when the torch head's
     [B,S,V] fp32 intermediates (about six of them alive at the peak of
-    forward + backward) fit in half the host's free memory, as the
-    CPU-baseline plan asks for configs 1-3; otherwise (configs 4, 5) a slice
+    forward + backward) fit in half the host's free memory (configs 1-3);
+    otherwise (configs 4, 5) a slice
     of rows, and the result is extrapolated (rows are independent)."""
     if rows:
         return min(rows, c["B"])
