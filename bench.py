@@ -612,7 +612,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
-                    help="BASELINE configuration (default config2, the one the metric is quoted on)")
+                    help="benchmark configuration (default config2, the one the metric is quoted on)")
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of the CPU-baseline sample (default: per workload)")
     ap.add_argument("--nccl-priority", choices=["high", "normal"], default="high",
@@ -897,7 +897,7 @@ def main(argv=None) -> int:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": DTYPE_NAME[c["dtype"]],
-        "data": f"synthetic (seeded; BASELINE {c['name'].split(' (')[0]} distributions)",
+        "data": f"synthetic (seeded; benchmark {c['name'].split(' (')[0]} distributions)",
         "config": {"workload": workload_desc(c),
                    "B": B, "S": S, "D": D, "V": V, "valid_tokens": T,
                    "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
